@@ -1,0 +1,105 @@
+"""ctypes binding of libfluxvla_b200.so (the C ABI in include/fluxvla_b200.h).
+
+The library is required: importing the ops without it raises, there is no
+fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, 'libfluxvla_b200.so')
+
+FVB_OK = 0
+EPI_BF16, EPI_F32_STORE, EPI_F32_ACC, EPI_GEGLU, EPI_QKV_ROPE = range(5)
+ACT_NONE, ACT_GELU_TANH, ACT_SILU = range(3)
+NORM_GEMMA_RMS, NORM_ADA_RMS, NORM_LAYER = range(3)
+
+
+class GemmArgs(C.Structure):
+    _fields_ = [('a', C.c_void_p), ('lda', C.c_int64), ('b', C.c_void_p),
+                ('ldb', C.c_int64), ('m', C.c_int32), ('n', C.c_int32),
+                ('k', C.c_int32), ('swap', C.c_int32),
+                ('epilogue', C.c_int32), ('act', C.c_int32),
+                ('split_k', C.c_int32), ('block_n', C.c_int32),
+                ('out', C.c_void_p), ('ldo', C.c_int64),
+                ('bias', C.c_void_p), ('gate', C.c_void_p),
+                ('alpha', C.c_float), ('row_add', C.c_void_p),
+                ('row_add_mod', C.c_int32), ('k_out', C.c_void_p),
+                ('v_out', C.c_void_p), ('ld_kv', C.c_int64),
+                ('n_heads', C.c_int32), ('head_dim', C.c_int32),
+                ('rope_cs', C.c_void_p), ('positions', C.c_void_p)]
+
+
+class AttnArgs(C.Structure):
+    _fields_ = [('q', C.c_void_p), ('q_row_stride', C.c_int64),
+                ('q_head_stride', C.c_int64), ('k', C.c_void_p),
+                ('k_row_stride', C.c_int64), ('k_head_stride', C.c_int64),
+                ('v', C.c_void_p), ('v_row_stride', C.c_int64),
+                ('v_head_stride', C.c_int64), ('o', C.c_void_p),
+                ('o_row_stride', C.c_int64), ('o_head_stride', C.c_int64),
+                ('n_q', C.c_int32), ('n_kv', C.c_int32),
+                ('heads', C.c_int32), ('group', C.c_int32),
+                ('batch', C.c_int32), ('q_batch_rows', C.c_int64),
+                ('kv_batch_rows', C.c_int64), ('head_dim', C.c_int32),
+                ('scale', C.c_float), ('key_valid', C.c_void_p),
+                ('n_prefix', C.c_int32), ('q_block', C.c_void_p),
+                ('k_block', C.c_void_p), ('kv_splits', C.c_int32),
+                ('workspace', C.c_void_p), ('workspace_bytes', C.c_int64)]
+
+
+EXPORTS = {
+    'fvb_gemm': (C.c_int, [C.POINTER(GemmArgs), C.c_void_p]),
+    'fvb_attention': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),
+    'fvb_attention_workspace_bytes': (C.c_int64, [C.POINTER(AttnArgs)]),
+    'fvb_attention_combine': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),
+    'fvb_norm': (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_void_p,
+                           C.c_int64, C.c_int32, C.c_int32, C.c_int32,
+                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                           C.c_void_p]),
+    'fvb_patchify': (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
+                               C.c_int32, C.c_void_p, C.c_void_p,
+                               C.c_void_p, C.c_int64, C.c_void_p]),
+    'fvb_embed_tokens': (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p,
+                                   C.c_int32, C.c_float, C.c_void_p,
+                                   C.c_int64, C.c_void_p]),
+    'fvb_small_linear': (C.c_int, [C.c_void_p, C.c_int64, C.c_int32,
+                                   C.c_int32, C.c_void_p, C.c_int64,
+                                   C.c_int32, C.c_void_p, C.c_int32,
+                                   C.c_int32, C.c_float, C.c_void_p,
+                                   C.c_int64, C.c_void_p]),
+    'fvb_get_device_status': (C.c_int, [C.POINTER(C.c_int), C.c_int]),
+    'fvb_last_error': (C.c_char_p, []),
+    'fvb_version': (C.c_int, []),
+    'fvb_launch_count': (C.c_int64, []),
+}
+
+_lib = None
+
+
+def lib():
+    """Load the library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f'{LIB_PATH} is missing: build it with '
+                '`python -m fluxvla_b200.build` (there is no fallback path)')
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in EXPORTS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+class FVBError(RuntimeError):
+    pass
+
+
+def check(rc: int):
+    if rc != FVB_OK:
+        raise FVBError(f'fluxvla_b200 error {rc}: '
+                       f'{lib().fvb_last_error().decode()}')

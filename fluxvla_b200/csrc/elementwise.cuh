@@ -1,0 +1,145 @@
+// Memory-bound helper kernels: row norms, image patchify, token embedding
+// gather, and the exact-f32 small linears of the action head.
+#pragma once
+
+#include "common.cuh"
+
+namespace fvb {
+
+constexpr int NORM_THREADS = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+  return t;
+}
+
+// One CTA per row; dim <= 8 * NORM_THREADS * 4 handled with a strided loop.
+__global__ void __launch_bounds__(NORM_THREADS)
+    norm_kernel(int mode, const float* __restrict__ x, long long ld_in,
+                void* __restrict__ out, long long ld_out, int out_f32,
+                int dim, const bf16* __restrict__ w,
+                const bf16* __restrict__ b, const float* __restrict__ mod,
+                float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const float* xr = x + (long long)row * ld_in;
+  float s = 0.f, ss = 0.f;
+  for (int i = threadIdx.x * 4; i < dim; i += NORM_THREADS * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    s += v.x + v.y + v.z + v.w;
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  float mean = 0.f, rstd;
+  if (mode == FVB_NORM_LAYER) {
+    mean = block_sum(s, red) / dim;
+    // two-pass variance for accuracy
+    float q = 0.f;
+    for (int i = threadIdx.x * 4; i < dim; i += NORM_THREADS * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + i);
+      q += (v.x - mean) * (v.x - mean) + (v.y - mean) * (v.y - mean) +
+           (v.z - mean) * (v.z - mean) + (v.w - mean) * (v.w - mean);
+    }
+    rstd = rsqrtf(block_sum(q, red) / dim + eps);
+  } else {
+    rstd = rsqrtf(block_sum(ss, red) / dim + eps);
+  }
+  for (int i = threadIdx.x * 4; i < dim; i += NORM_THREADS * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    float y[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = i + e;
+      float t = (y[e] - mean) * rstd;
+      if (mode == FVB_NORM_GEMMA_RMS) {
+        t *= 1.f + __bfloat162float(w[c]);
+      } else if (mode == FVB_NORM_ADA_RMS) {
+        t = t * (1.f + mod[c]) + mod[dim + c];
+      } else {
+        t = t * __bfloat162float(w[c]) + __bfloat162float(b[c]);
+      }
+      y[e] = t;
+    }
+    if (out_f32) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) +
+                                 (long long)row * ld_out + i) =
+          make_float4(y[0], y[1], y[2], y[3]);
+    } else {
+      uint2 pk = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+      *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(out) +
+                                (long long)row * ld_out + i) = pk;
+    }
+  }
+}
+
+// uint8 HWC images -> normalised bf16 patch rows.  One CTA per patch row.
+__global__ void patchify_kernel(const uint8_t* __restrict__ img, int H, int W,
+                                int P, float m0, float m1, float m2, float s0,
+                                float s1, float s2, bf16* __restrict__ out,
+                                long long ldo) {
+  const int gw = W / P, gh = H / P;
+  const int r = blockIdx.x;
+  const int v = r / (gh * gw), py = (r / gw) % gh, px = r % gw;
+  const int K = 3 * P * P;
+  bf16* o = out + (long long)r * ldo;
+  for (int col = threadIdx.x; col < ldo; col += blockDim.x) {
+    float val = 0.f;
+    if (col < K) {
+      const int c = col / (P * P), ky = (col / P) % P, kx = col % P;
+      const int y = py * P + ky, x = px * P + kx;
+      const float raw = img[(((long long)v * H + y) * W + x) * 3 + c];
+      const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
+      const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+      val = (raw - mean) / (sd + 1e-8f);
+    }
+    o[col] = __float2bfloat16(val);
+  }
+}
+
+__global__ void embed_kernel(const long long* __restrict__ ids,
+                             const bf16* __restrict__ table, int dim,
+                             float scale, float* __restrict__ out,
+                             long long ldo) {
+  const long long id = ids[blockIdx.x];
+  const bf16* src = table + id * dim;
+  float* dst = out + (long long)blockIdx.x * ldo;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x)
+    dst[i] = __bfloat162float(src[i]) * scale;
+}
+
+// One warp per output element (t, n): y = act(x[t,:] . W[n,:] + bias[n]).
+__global__ void small_linear_kernel(const float* __restrict__ x, long long ldx,
+                                    int T, int K, const bf16* __restrict__ w,
+                                    long long ldw, int N,
+                                    const float* __restrict__ bias, int act,
+                                    int mode, float alpha, void* out,
+                                    long long ldo) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= T * N) return;
+  const int t = gw / N, n = gw % N;
+  const float* xr = x + (long long)t * ldx;
+  const bf16* wr = w + (long long)n * ldw;
+  float acc = 0.f;
+  for (int k = lane; k < K; k += 32) acc += xr[k] * __bfloat162float(wr[k]);
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    float y = acc + (bias ? bias[n] : 0.f);
+    if (act == FVB_ACT_SILU) y = silu_f(y);
+    else if (act == FVB_ACT_GELU_TANH) y = gelu_tanh_f(y);
+    if (mode == 0)
+      reinterpret_cast<float*>(out)[(long long)t * ldo + n] = y;
+    else if (mode == 1)
+      reinterpret_cast<bf16*>(out)[(long long)t * ldo + n] =
+          __float2bfloat16(y);
+    else
+      reinterpret_cast<float*>(out)[(long long)t * ldo + n] += alpha * y;
+  }
+}
+
+}  // namespace fvb

@@ -1,0 +1,346 @@
+// C ABI of the fluxvla_b200 kernels (declared in include/fluxvla_b200.h).
+// Host side: argument checks, TMA tensor-map encoding, grid sizing, launch.
+// No entry point allocates, synchronises or exits.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "elementwise.cuh"
+#include "gemm_tc.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+std::atomic<long long> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "%s: launch failed: %s", what,
+                cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return FVB_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
+                                  void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p,
+                                cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over [rows, k] (row stride ld elements), box
+// [box_rows, 64] with the 128-byte swizzle; out-of-range reads fill zeros.
+int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t k,
+             int64_t ld, int box_rows) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return fail(FVB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FVB_ERR_INVALID_ARG, "tensor map encode failed (%d)", (int)r);
+  return FVB_OK;
+}
+
+template <int BN>
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
+                const fvb::GemmDev& d, dim3 grid, cudaStream_t st) {
+  using C = fvb::GemmCfg<BN>;
+  auto kern = fvb::gemm_tc_kernel<BN, C::STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM) != cudaSuccess)
+      return fail(FVB_ERR_CUDA, "gemm smem attribute: %s",
+                  cudaGetErrorString(cudaGetLastError()));
+    attr = true;
+  }
+  kern<<<grid, fvb::GEMM_THREADS, C::SMEM, st>>>(ma, mb, d);
+  return check_launch("fvb_gemm");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int fvb_version(void) { return 1; }
+const char* fvb_last_error(void) { return g_err; }
+int64_t fvb_launch_count(void) { return g_launches.load(); }
+
+int fvb_get_device_status(int* status, int reset) {
+  if (!status) return fail(FVB_ERR_INVALID_ARG, "status is NULL");
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_fvb_device_status, sizeof(int));
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "read status: %s", cudaGetErrorString(e));
+  if (reset) {
+    int z = 0;
+    e = cudaMemcpyToSymbol(g_fvb_device_status, &z, sizeof(int));
+    if (e != cudaSuccess)
+      return fail(FVB_ERR_CUDA, "reset status: %s", cudaGetErrorString(e));
+  }
+  return FVB_OK;
+}
+
+int fvb_gemm(const fvb_gemm_args* a, void* stream) {
+  if (!a) return fail(FVB_ERR_INVALID_ARG, "args is NULL");
+  if (!a->a || !a->b || !a->out)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: NULL operand");
+  if (a->m <= 0 || a->n <= 0 || a->k <= 0)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: bad shape %d %d %d", a->m,
+                a->n, a->k);
+  if (a->k % 8 || a->lda % 8 || a->ldb % 8 || a->lda < a->k || a->ldb < a->k)
+    return fail(FVB_ERR_INVALID_ARG,
+                "fvb_gemm: k / lda / ldb must be multiples of 8 and >= k");
+  if (!aligned16(a->a) || !aligned16(a->b))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: operands must be 16B aligned");
+  if (a->epilogue < FVB_EPI_BF16 || a->epilogue > FVB_EPI_QKV_ROPE)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: bad epilogue %d", a->epilogue);
+  const int split = a->split_k > 1 ? a->split_k : 1;
+  if (split > 1 && a->epilogue != FVB_EPI_F32_ACC)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: split_k needs FVB_EPI_F32_ACC");
+  const int n_feat = a->swap ? a->m : a->n;
+  if (a->epilogue == FVB_EPI_GEGLU && (n_feat & 1))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: GEGLU needs an even feature count");
+  if (a->epilogue == FVB_EPI_QKV_ROPE) {
+    if (!a->k_out || !a->v_out || !a->rope_cs || !a->positions ||
+        a->head_dim % 16 || a->head_dim <= 0 ||
+        n_feat != (a->n_heads + 2) * a->head_dim)
+      return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: bad QKV_ROPE arguments");
+    if (!a->swap && (a->ldo % 8 || a->ld_kv % 8 || !aligned16(a->out) ||
+                     !aligned16(a->k_out) || !aligned16(a->v_out)))
+      return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: QKV outputs must be 16B aligned");
+  }
+  if (a->epilogue == FVB_EPI_GEGLU && !a->swap &&
+      (a->ldo % 8 || !aligned16(a->out)))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: GEGLU output must be 16B aligned");
+  if (a->row_add && a->row_add_mod <= 0)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: row_add_mod must be > 0");
+
+  int bn = a->block_n;
+  if (bn == 0) bn = a->swap ? 64 : 128;
+  if (bn != 64 && bn != 128 && bn != 256)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: block_n must be 64/128/256");
+
+  CUtensorMap ma, mb;
+  int r = make_map(&ma, a->a, a->m, a->k, a->lda, fvb::GEMM_BM);
+  if (r) return r;
+  r = make_map(&mb, a->b, a->n, a->k, a->ldb, bn);
+  if (r) return r;
+
+  fvb::GemmDev d;
+  d.m = a->m; d.n = a->n; d.k = a->k;
+  d.swap = a->swap; d.epi = a->epilogue; d.act = a->act;
+  d.k_tiles = (a->k + fvb::GEMM_BK - 1) / fvb::GEMM_BK;
+  d.kt_per_split = (d.k_tiles + split - 1) / split;
+  d.split = (d.k_tiles + d.kt_per_split - 1) / d.kt_per_split;
+  d.out = a->out; d.ldo = a->ldo;
+  d.bias = a->bias; d.gate = a->gate; d.alpha = a->alpha;
+  d.row_add = reinterpret_cast<const bf16*>(a->row_add);
+  d.row_add_mod = a->row_add_mod;
+  d.k_out = reinterpret_cast<bf16*>(a->k_out);
+  d.v_out = reinterpret_cast<bf16*>(a->v_out);
+  d.ld_kv = a->ld_kv; d.n_heads = a->n_heads; d.head_dim = a->head_dim;
+  d.rope_cs = a->rope_cs; d.positions = a->positions;
+
+  dim3 grid((a->m + fvb::GEMM_BM - 1) / fvb::GEMM_BM, (a->n + bn - 1) / bn,
+            d.split);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (bn == 64) return launch_gemm<64>(ma, mb, d, grid, st);
+  if (bn == 128) return launch_gemm<128>(ma, mb, d, grid, st);
+  return launch_gemm<256>(ma, mb, d, grid, st);
+}
+
+static int attn_prepare(const fvb_attn_args* a, fvb::AttnDev* d) {
+  if (!a) return fail(FVB_ERR_INVALID_ARG, "args is NULL");
+  if (!a->q || !a->k || !a->v || !a->o)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_attention: NULL operand");
+  if (a->head_dim != 256 && a->head_dim != 72)
+    return fail(FVB_ERR_UNSUPPORTED, "fvb_attention: head_dim %d (256 or 72)",
+                a->head_dim);
+  if (a->n_q <= 0 || a->n_kv <= 0 || a->heads <= 0 || a->group <= 0 ||
+      a->heads % a->group || a->batch <= 0)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_attention: bad shape");
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) ||
+      a->q_row_stride % 8 || a->k_row_stride % 8 || a->v_row_stride % 8 ||
+      a->q_head_stride % 8 || a->k_head_stride % 8 || a->v_head_stride % 8)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_attention: 16B alignment required");
+  if (a->o_row_stride % 2 || a->o_head_stride % 2)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_attention: output strides must be even");
+  if (a->n_prefix < a->n_kv && a->q_block && !a->k_block)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_attention: q_block needs k_block");
+  d->q = (const bf16*)a->q; d->q_rs = a->q_row_stride; d->q_hs = a->q_head_stride;
+  d->k = (const bf16*)a->k; d->k_rs = a->k_row_stride; d->k_hs = a->k_head_stride;
+  d->v = (const bf16*)a->v; d->v_rs = a->v_row_stride; d->v_hs = a->v_head_stride;
+  d->o = (bf16*)a->o; d->o_rs = a->o_row_stride; d->o_hs = a->o_head_stride;
+  d->n_q = a->n_q; d->n_kv = a->n_kv; d->heads = a->heads;
+  d->group = a->group; d->batch = a->batch;
+  d->q_br = a->q_batch_rows; d->kv_br = a->kv_batch_rows;
+  d->scale_log2 = a->scale * 1.4426950408889634f;
+  d->key_valid = a->key_valid; d->n_prefix = a->n_prefix;
+  d->q_block = a->q_block; d->k_block = a->k_block;
+  const int nkb = (a->n_kv + fvb::ATT_BN - 1) / fvb::ATT_BN;
+  int splits = a->kv_splits > 1 ? a->kv_splits : 1;
+  if (splits > nkb) splits = nkb;
+  d->blocks_per_split = (nkb + splits - 1) / splits;
+  d->splits = (nkb + d->blocks_per_split - 1) / d->blocks_per_split;
+  const long long rows = (long long)a->batch * a->heads * a->n_q;
+  d->part_o = (float*)a->workspace;
+  d->part_ml = d->part_o ? d->part_o + (long long)d->splits * rows * a->head_dim
+                         : nullptr;
+  return FVB_OK;
+}
+
+int64_t fvb_attention_workspace_bytes(const fvb_attn_args* a) {
+  fvb::AttnDev d;
+  if (attn_prepare(a, &d)) return -1;
+  if (d.splits == 1) return 0;
+  const long long rows = (long long)a->batch * a->heads * a->n_q;
+  return (long long)d.splits * rows * (a->head_dim + 2) * sizeof(float);
+}
+
+int fvb_attention(const fvb_attn_args* a, void* stream) {
+  fvb::AttnDev d;
+  int r = attn_prepare(a, &d);
+  if (r) return r;
+  if (d.splits > 1) {
+    const long long need = fvb_attention_workspace_bytes(a);
+    if (!a->workspace || a->workspace_bytes < need || !aligned16(a->workspace))
+      return fail(FVB_ERR_WORKSPACE, "fvb_attention: workspace needs %lld bytes",
+                  need);
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid((a->n_q + fvb::ATT_BM - 1) / fvb::ATT_BM, a->heads,
+            a->batch * d.splits);
+  if (a->head_dim == 256) {
+    constexpr int S = fvb::attn_smem_bytes<256, 256>();
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(fvb::attn_kernel<256, 256>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, S);
+      attr = true;
+    }
+    fvb::attn_kernel<256, 256><<<grid, fvb::ATT_THREADS, S, st>>>(d);
+  } else {
+    constexpr int S = fvb::attn_smem_bytes<72, 80>();
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(fvb::attn_kernel<72, 80>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, S);
+      attr = true;
+    }
+    fvb::attn_kernel<72, 80><<<grid, fvb::ATT_THREADS, S, st>>>(d);
+  }
+  return check_launch("fvb_attention");
+}
+
+int fvb_attention_combine(const fvb_attn_args* a, void* stream) {
+  fvb::AttnDev d;
+  int r = attn_prepare(a, &d);
+  if (r) return r;
+  if (d.splits == 1) return FVB_OK;
+  if (!a->workspace) return fail(FVB_ERR_WORKSPACE, "combine: no workspace");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int rows = a->batch * a->heads * a->n_q;
+  if (a->head_dim == 256)
+    fvb::attn_combine_kernel<256><<<rows, 256, 0, st>>>(d);
+  else
+    fvb::attn_combine_kernel<72><<<rows, 96, 0, st>>>(d);
+  return check_launch("fvb_attention_combine");
+}
+
+int fvb_norm(int32_t mode, const float* x, int64_t ld_in, void* out,
+             int64_t ld_out, int32_t out_f32, int32_t rows, int32_t dim,
+             const void* w, const void* b, const float* mod, float eps,
+             void* stream) {
+  if (!x || !out || rows <= 0 || dim <= 0 || dim % 4 || ld_in % 4 ||
+      ld_out % 4)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm: bad arguments");
+  if (mode == FVB_NORM_GEMMA_RMS && !w)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm: weight required");
+  if (mode == FVB_NORM_ADA_RMS && !mod)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm: modulation required");
+  if (mode == FVB_NORM_LAYER && (!w || !b))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm: weight and bias required");
+  if (mode < 0 || mode > 2)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm: bad mode");
+  fvb::norm_kernel<<<rows, fvb::NORM_THREADS, 0,
+                     reinterpret_cast<cudaStream_t>(stream)>>>(
+      mode, x, ld_in, out, ld_out, out_f32, dim, (const bf16*)w,
+      (const bf16*)b, mod, eps);
+  return check_launch("fvb_norm");
+}
+
+int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
+                 int32_t width, int32_t patch, const float* mean3,
+                 const float* std3, void* out, int64_t ldo, void* stream) {
+  if (!images || !out || !mean3 || !std3 || views <= 0 || patch <= 0 ||
+      height % patch || width % patch || ldo < 3 * patch * patch)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_patchify: bad arguments");
+  const int rows = views * (height / patch) * (width / patch);
+  fvb::patchify_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      images, height, width, patch, mean3[0], mean3[1], mean3[2], std3[0],
+      std3[1], std3[2], (bf16*)out, ldo);
+  return check_launch("fvb_patchify");
+}
+
+int fvb_embed_tokens(const int64_t* ids, int32_t n, const void* table,
+                     int32_t dim, float scale, float* out, int64_t ldo,
+                     void* stream) {
+  if (!ids || !table || !out || n <= 0 || dim <= 0)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_embed_tokens: bad arguments");
+  fvb::embed_kernel<<<n, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      (const long long*)ids, (const bf16*)table, dim, scale, out, ldo);
+  return check_launch("fvb_embed_tokens");
+}
+
+int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
+                     const void* w, int64_t ldw, int32_t n, const float* bias,
+                     int32_t act, int32_t mode, float alpha, void* out,
+                     int64_t ldo, void* stream) {
+  if (!x || !w || !out || t <= 0 || k <= 0 || n <= 0 || mode < 0 || mode > 2)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_small_linear: bad arguments");
+  const long long warps = (long long)t * n;
+  const int threads = 256;
+  const long long blocks = (warps * 32 + threads - 1) / threads;
+  fvb::small_linear_kernel<<<(unsigned)blocks, threads, 0,
+                             reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, ldx, t, k, (const bf16*)w, ldw, n, bias, act, mode, alpha, out, ldo);
+  return check_launch("fvb_small_linear");
+}
+
+}  // extern "C"

@@ -1,0 +1,156 @@
+"""torch-facing wrappers over the C ABI (one call = one or two kernel launches
+on the current torch CUDA stream).  Every wrapper takes caller-allocated
+outputs, like the reference's fluxvla/ops/atomic_ops.py functions; nothing
+here allocates device memory except where a docstring says so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import (ACT_NONE, EPI_BF16, EPI_F32_ACC, EPI_F32_STORE,
+                   EPI_GEGLU, EPI_QKV_ROPE, AttnArgs, GemmArgs, check)
+
+BF16 = torch.bfloat16
+F32 = torch.float32
+
+
+def _ptr(t: Optional[torch.Tensor]) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _rowmajor(t: torch.Tensor, name: str, dtype) -> int:
+    if t.dtype != dtype:
+        raise TypeError(f'{name}: expected {dtype}, got {t.dtype}')
+    if not t.is_cuda:
+        raise ValueError(f'{name}: must be a CUDA tensor')
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f'{name}: expected a 2-D row-major view')
+    return t.stride(0)
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
+         epilogue: int = EPI_BF16, swap: bool = False, act: int = ACT_NONE,
+         bias: Optional[torch.Tensor] = None,
+         gate: Optional[torch.Tensor] = None, alpha: float = 1.0,
+         split_k: int = 1, block_n: int = 0,
+         row_add: Optional[torch.Tensor] = None, row_add_mod: int = 0,
+         k_out: Optional[torch.Tensor] = None,
+         v_out: Optional[torch.Tensor] = None, n_heads: int = 0,
+         head_dim: int = 0, rope_cs: Optional[torch.Tensor] = None,
+         positions: Optional[torch.Tensor] = None) -> None:
+    """C[M,N] = A[M,K] @ B[N,K]^T with a fused epilogue (see fvb_gemm)."""
+    lda = _rowmajor(a, 'a', BF16)
+    ldb = _rowmajor(b, 'b', BF16)
+    if a.shape[1] != b.shape[1]:
+        raise ValueError(f'K mismatch {a.shape} {b.shape}')
+    out_dtype = F32 if epilogue in (EPI_F32_STORE, EPI_F32_ACC) else BF16
+    ldo = _rowmajor(out, 'out', out_dtype)
+    for t, n in ((bias, 'bias'), (gate, 'gate')):
+        if t is not None and (t.dtype != F32 or not t.is_contiguous()):
+            raise TypeError(f'{n}: expected contiguous float32')
+    args = GemmArgs(a=_ptr(a), lda=lda, b=_ptr(b), ldb=ldb, m=a.shape[0],
+                    n=b.shape[0], k=a.shape[1], swap=int(swap),
+                    epilogue=epilogue, act=act, split_k=split_k,
+                    block_n=block_n, out=_ptr(out), ldo=ldo, bias=_ptr(bias),
+                    gate=_ptr(gate), alpha=alpha, row_add=_ptr(row_add),
+                    row_add_mod=row_add_mod, k_out=_ptr(k_out),
+                    v_out=_ptr(v_out),
+                    ld_kv=0 if k_out is None else k_out.stride(0),
+                    n_heads=n_heads, head_dim=head_dim, rope_cs=_ptr(rope_cs),
+                    positions=_ptr(positions))
+    check(_lib.lib().fvb_gemm(C.byref(args), _stream()))
+
+
+def attn_args(q, k, v, o, *, n_q, n_kv, heads, group, head_dim, scale,
+              q_row_stride, q_head_stride, k_row_stride, k_head_stride,
+              v_row_stride, v_head_stride, o_row_stride, o_head_stride,
+              batch=1, q_batch_rows=0, kv_batch_rows=0, key_valid=None,
+              n_prefix=None, q_block=None, k_block=None, kv_splits=1,
+              workspace=None) -> AttnArgs:
+    return AttnArgs(
+        q=_ptr(q), q_row_stride=q_row_stride, q_head_stride=q_head_stride,
+        k=_ptr(k), k_row_stride=k_row_stride, k_head_stride=k_head_stride,
+        v=_ptr(v), v_row_stride=v_row_stride, v_head_stride=v_head_stride,
+        o=_ptr(o), o_row_stride=o_row_stride, o_head_stride=o_head_stride,
+        n_q=n_q, n_kv=n_kv, heads=heads, group=group, batch=batch,
+        q_batch_rows=q_batch_rows, kv_batch_rows=kv_batch_rows,
+        head_dim=head_dim, scale=scale, key_valid=_ptr(key_valid),
+        n_prefix=n_kv if n_prefix is None else n_prefix,
+        q_block=_ptr(q_block), k_block=_ptr(k_block), kv_splits=kv_splits,
+        workspace=_ptr(workspace),
+        workspace_bytes=0 if workspace is None else workspace.numel() *
+        workspace.element_size())
+
+
+def attention_workspace_bytes(args: AttnArgs) -> int:
+    n = _lib.lib().fvb_attention_workspace_bytes(C.byref(args))
+    if n < 0:
+        check(1)
+    return n
+
+
+def attention(args: AttnArgs) -> None:
+    """Fused attention; with kv_splits > 1 also launches the combine."""
+    L = _lib.lib()
+    check(L.fvb_attention(C.byref(args), _stream()))
+    if args.kv_splits > 1:
+        check(L.fvb_attention_combine(C.byref(args), _stream()))
+
+
+def norm(mode: int, x: torch.Tensor, out: torch.Tensor, *, w=None, b=None,
+         mod=None, eps: float = 1e-6) -> None:
+    ld_in = _rowmajor(x, 'x', F32)
+    out_f32 = out.dtype == F32
+    ld_out = _rowmajor(out, 'out', F32 if out_f32 else BF16)
+    rows, dim = x.shape
+    check(_lib.lib().fvb_norm(mode, _ptr(x), ld_in, _ptr(out), ld_out,
+                              int(out_f32), rows, dim, _ptr(w), _ptr(b),
+                              _ptr(mod), eps, _stream()))
+
+
+def patchify(images_u8: torch.Tensor, patch: int, mean3, std3,
+             out: torch.Tensor) -> None:
+    """mean3 / std3: three host floats each."""
+    V, H, W, _ = images_u8.shape
+    m = (C.c_float * 3)(*[float(x) for x in mean3])
+    s = (C.c_float * 3)(*[float(x) for x in std3])
+    check(_lib.lib().fvb_patchify(_ptr(images_u8), V, H, W, patch,
+                                  C.cast(m, C.c_void_p), C.cast(s, C.c_void_p),
+                                  _ptr(out), out.stride(0), _stream()))
+
+
+def embed_tokens(ids: torch.Tensor, table: torch.Tensor, scale: float,
+                 out: torch.Tensor) -> None:
+    check(_lib.lib().fvb_embed_tokens(_ptr(ids), ids.numel(), _ptr(table),
+                                      table.shape[1], scale, _ptr(out),
+                                      out.stride(0), _stream()))
+
+
+def small_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *,
+                 bias=None, act: int = ACT_NONE, mode: int = 0,
+                 alpha: float = 1.0, k: Optional[int] = None) -> None:
+    """y = act(x @ w[:, :k]^T + bias); mode 0 store f32, 1 store bf16,
+    2 out += alpha*y (f32)."""
+    T, K = x.shape[0], (k or x.shape[1])
+    check(_lib.lib().fvb_small_linear(_ptr(x), x.stride(0), T, K, _ptr(w),
+                                      w.stride(0), w.shape[0], _ptr(bias),
+                                      act, mode, alpha, _ptr(out),
+                                      out.stride(0), _stream()))
+
+
+def device_status(reset: bool = False) -> int:
+    s = C.c_int(0)
+    check(_lib.lib().fvb_get_device_status(C.byref(s), int(reset)))
+    return s.value
+
+
+def launch_count() -> int:
+    return _lib.lib().fvb_launch_count()

@@ -1,0 +1,194 @@
+/*
+ * fluxvla_b200 C ABI.
+ *
+ * The B200 (sm_100a) kernels of FluxVLA's PI0 / PI0.5 inference path behind
+ * plain C entry points: raw device pointers, element counts and strides, a
+ * CUDA stream passed as `void*` (NULL = legacy default stream).  Nothing here
+ * allocates device memory, synchronises the device or exits the process;
+ * every entry point returns FVB_OK or an FVB_ERR_* code and leaves a message
+ * for fvb_last_error().  Kernels never trap: a device-side wait that runs
+ * out of time sets a status word read by fvb_get_device_status().
+ *
+ * All matrices are row-major.  "bf16" pointers are IEEE bfloat16.  Weights
+ * use the nn.Linear [out_features, in_features] layout (K-major), packed by
+ * fluxvla_b200/pack.py where an epilogue pairs output features.
+ *
+ * Each entry point names the reference interface it replaces
+ * (paths relative to the FluxVLA project root).
+ */
+#ifndef FLUXVLA_B200_H_
+#define FLUXVLA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FVB_OK 0
+#define FVB_ERR_INVALID_ARG 1
+#define FVB_ERR_UNSUPPORTED 2
+#define FVB_ERR_CUDA 3
+#define FVB_ERR_DEVICE_TIMEOUT 4
+#define FVB_ERR_WORKSPACE 5
+
+/* GEMM epilogues (fvb_gemm_args.epilogue).  t = token row, f = feature. */
+#define FVB_EPI_BF16 0      /* out_bf16[t,f] = act(alpha*acc + bias[f])      */
+#define FVB_EPI_F32_STORE 1 /* out_f32[t,f] = acc + bias[f] + row_add[t%mod,f] */
+#define FVB_EPI_F32_ACC 2   /* out_f32[t,f] += alpha*gate[f]*(acc + bias[f]) */
+#define FVB_EPI_GEGLU 3     /* out_bf16[t,i] = gelu_tanh(acc[2i]) * acc[2i+1] */
+#define FVB_EPI_QKV_ROPE 4  /* q -> out (RoPE), k -> k_out (RoPE), v -> v_out */
+
+#define FVB_ACT_NONE 0
+#define FVB_ACT_GELU_TANH 1
+#define FVB_ACT_SILU 2
+
+/* Norm modes (fvb_norm). */
+#define FVB_NORM_GEMMA_RMS 0 /* x*rsqrt(mean(x^2)+eps)*(1+w)               */
+#define FVB_NORM_ADA_RMS 1   /* x*rsqrt(mean(x^2)+eps)*(1+scale)+shift     */
+#define FVB_NORM_LAYER 2     /* (x-mean)*rsqrt(var+eps)*w + b              */
+
+typedef struct fvb_gemm_args {
+  /* C[M,N] = A[M,K] * B[N,K]^T, bf16 operands, f32 accumulation.         */
+  const void* a; /* bf16 [m, lda] */
+  int64_t lda;   /* elements; multiple of 8 */
+  const void* b; /* bf16 [n, ldb] */
+  int64_t ldb;
+  int32_t m, n, k; /* k multiple of 8 */
+  /* swap = 0: A rows are tokens and B rows are features (prefill).
+   * swap = 1: A rows are features (weights) and B rows are tokens; used for
+   *           the denoise loop where tokens <= 64.                         */
+  int32_t swap;
+  int32_t epilogue; /* FVB_EPI_* */
+  int32_t act;      /* FVB_ACT_*, FVB_EPI_BF16 only */
+  int32_t split_k;  /* >1 only with FVB_EPI_F32_ACC (atomic accumulation) */
+  int32_t block_n;  /* 0 = auto, else 64 / 128 / 256 */
+  void* out;        /* see epilogues */
+  int64_t ldo;      /* elements */
+  const float* bias;    /* [features] or NULL */
+  const float* gate;    /* [features] or NULL (FVB_EPI_F32_ACC) */
+  float alpha;          /* FVB_EPI_BF16 / FVB_EPI_F32_ACC scale */
+  const void* row_add;  /* bf16 [row_add_mod, features] or NULL */
+  int32_t row_add_mod;
+  /* FVB_EPI_QKV_ROPE: packed features = [n_heads*head_dim q | head_dim k |
+   * head_dim v]; q and k rows pair-interleaved (packed row 2i = dim i,
+   * 2i+1 = dim i + head_dim/2).  q goes to out [t, n_heads*head_dim], k/v
+   * to k_out/v_out [t, head_dim] with row stride ld_kv.                   */
+  void* k_out;
+  void* v_out;
+  int64_t ld_kv;
+  int32_t n_heads;
+  int32_t head_dim;
+  const float* rope_cs;      /* [max_pos, head_dim/2, 2] (cos, sin) f32 */
+  const int32_t* positions;  /* [tokens] */
+} fvb_gemm_args;
+
+/* tcgen05/TMEM tensor-core GEMM with fused epilogues.
+ * Replaces: matmul_bias_cuda (fluxvla/ops/cuda/matmul_bias/matmul_bias.py:19,
+ * src/matmul_bias_forward_cuda.cu:58), and the Triton GEMMs launched through
+ * fluxvla/ops/atomic_ops.py: matmul_bias_res :81, layer_norm_matmul_bias_gelu
+ * :85 (GEMM half), matmul_split_k_bias_res :109, rms_matmul_qkv_rope :157
+ * (GEMM half, matmul_n_2048_2560_qkv_rope attention_triton_ops.py:149),
+ * matmul_res :174, rms_matmul_gate :198 (matmul_small_gate
+ * matmul_triton_ops.py:763), matmul_bias_silu :231, matmul_qkv_rope :309,
+ * matmul_res_gate :345, matmul_gate :375.                                  */
+int fvb_gemm(const fvb_gemm_args* args, void* stream);
+
+typedef struct fvb_attn_args {
+  /* Element (row r, head h, dim d) of Q is
+   * q[(batch*q_batch_rows + r)*q_row_stride + h*q_head_stride + d]; K and V
+   * use kv head (h / group) with their own strides; O like Q.             */
+  const void* q;
+  int64_t q_row_stride, q_head_stride;
+  const void* k;
+  int64_t k_row_stride, k_head_stride;
+  const void* v;
+  int64_t v_row_stride, v_head_stride;
+  void* o;
+  int64_t o_row_stride, o_head_stride;
+  int32_t n_q;      /* query rows per (batch, head) */
+  int32_t n_kv;     /* keys */
+  int32_t heads;    /* query heads */
+  int32_t group;    /* query heads per kv head */
+  int32_t batch;    /* independent batches (SigLIP views) */
+  int64_t q_batch_rows, kv_batch_rows;
+  int32_t head_dim; /* 256 or 72 */
+  float scale;
+  /* mask: key j < n_prefix is visible iff key_valid == NULL or key_valid[j];
+   * key j >= n_prefix is visible to query i iff
+   * k_block[j - n_prefix] <= q_block[i] (q_block NULL: all visible).      */
+  const uint8_t* key_valid;
+  int32_t n_prefix;
+  const int32_t* q_block;
+  const int32_t* k_block;
+  /* split over keys: kv_splits > 1 writes partial results to workspace and
+   * needs fvb_attention_combine; workspace_bytes from
+   * fvb_attention_workspace_bytes().                                       */
+  int32_t kv_splits;
+  void* workspace;
+  int64_t workspace_bytes;
+} fvb_attn_args;
+
+/* Fused masked MQA/MHA attention (flash-style online softmax; no logits in
+ * HBM).  Replaces: matmul_abT_scale + softmax_kernel_masklen /
+ * softmax_kernel_prefix_suffix + matmul_attn_v
+ * (fluxvla/ops/triton/attention_triton_ops.py:5,80,111;
+ * fluxvla/ops/atomic_ops.py:211) and AttnMultiKey (atomic_ops.py:67).     */
+int fvb_attention(const fvb_attn_args* args, void* stream);
+int64_t fvb_attention_workspace_bytes(const fvb_attn_args* args);
+/* Merge of the kv_splits partial results into args->o. */
+int fvb_attention_combine(const fvb_attn_args* args, void* stream);
+
+/* Row normalisation, f32 input rows [rows, dim] (row stride ld_in), output
+ * bf16 or f32 (out_f32 != 0) with row stride ld_out.
+ * mode FVB_NORM_GEMMA_RMS: w = bf16 [dim]; FVB_NORM_ADA_RMS: mod = f32
+ * [2*dim] (scale | shift); FVB_NORM_LAYER: w, b = bf16 [dim].
+ * Replaces: rms_norm_kernel (fluxvla/ops/triton/norm_triton_ops.py:317),
+ * adarms_norm_kernel (:355), layer_norm_small_kernel (:90).              */
+int fvb_norm(int32_t mode, const float* x, int64_t ld_in, void* out,
+             int64_t ld_out, int32_t out_f32, int32_t rows, int32_t dim,
+             const void* w, const void* b, const float* mod, float eps,
+             void* stream);
+
+/* Image normalisation + patch extraction: uint8 HWC images [views, H, W, 3]
+ * -> bf16 patch rows [views*(H/p)*(W/p), ldo] with column c*p*p + ky*p + kx
+ * holding (x - mean[c]) / (std[c] + 1e-8); columns >= 3*p*p are zeroed.
+ * mean3 / std3 are HOST arrays of 3 floats (read at call time).
+ * Replaces: NormalizeImages (fluxvla/transforms/transform_images.py:313)
+ * and the im2col half of conv2d_embed_res (fluxvla/ops/atomic_ops.py:36). */
+int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
+                 int32_t width, int32_t patch, const float* mean3,
+                 const float* std3, void* out, int64_t ldo, void* stream);
+
+/* out_f32[i, :] = table_bf16[ids[i], :] * scale.
+ * Replaces: embed_tokens(...) * sqrt(width)
+ * (fluxvla/models/vlas/pi0_flowmatching.py:233-237).                      */
+int fvb_embed_tokens(const int64_t* ids, int32_t n, const void* table,
+                     int32_t dim, float scale, float* out, int64_t ldo,
+                     void* stream);
+
+/* Small exact-f32 linear for the K<=64 / N<=64 projections of the action
+ * head: y[t,n] = act(sum_k x[t,k] * W[n,k] + bias[n]) with x f32 [T, ldx],
+ * W bf16 [N, ldw].  mode 0: store f32, 1: store bf16, 2: Euler update
+ * out_f32[t,n] += alpha * y[t,n].
+ * Replaces: matmul_bias_small / matmul_bias_silu
+ * (fluxvla/ops/atomic_ops.py:231,251) for state_proj / action_in_proj /
+ * action_out_proj / time MLP, and the Euler step
+ * (fluxvla/models/vlas/pi0_flowmatching.py:646).                         */
+int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
+                     const void* w, int64_t ldw, int32_t n,
+                     const float* bias, int32_t act, int32_t mode,
+                     float alpha, void* out, int64_t ldo, void* stream);
+
+/* Status and diagnostics. */
+int fvb_get_device_status(int* status, int reset);
+const char* fvb_last_error(void);
+int fvb_version(void);
+/* Number of kernels this library has launched since load (host counter). */
+int64_t fvb_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLUXVLA_B200_H_ */

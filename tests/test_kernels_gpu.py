@@ -1,0 +1,300 @@
+"""Per-kernel numerics of the CUDA path against plain PyTorch fp32 references
+of the same op (bf16 inputs upcast).  Tolerances: bf16 outputs 1e-2 abs +
+1e-2 rel of the output scale; f32 outputs 2e-3 rel."""
+import math
+
+import pytest
+import torch
+
+from fluxvla_b200 import ops
+from fluxvla_b200._lib import (ACT_GELU_TANH, ACT_NONE, ACT_SILU, EPI_BF16,
+                               EPI_F32_ACC, EPI_F32_STORE, EPI_GEGLU,
+                               EPI_QKV_ROPE, NORM_ADA_RMS, NORM_GEMMA_RMS,
+                               NORM_LAYER)
+from fluxvla_b200.pack import pack_geglu, pack_qkv, rope_table
+
+pytestmark = pytest.mark.gpu
+DEV = 'cuda'
+
+
+def close(out, ref, tol=1e-2):
+    out, ref = out.float(), ref.float()
+    scale = ref.abs().max().item() + 1e-6
+    err = (out - ref).abs().max().item()
+    assert err <= tol * scale + tol * 0.1, f'max err {err} scale {scale}'
+
+
+def rnd(*s, std=1.0, dtype=torch.bfloat16):
+    return (torch.randn(*s, device=DEV) * std).to(dtype)
+
+
+@pytest.mark.parametrize('m,n,k,bn', [(816, 2560, 2048, 128), (3, 40, 64, 0),
+                                      (130, 300, 592, 64), (768, 4304, 1152, 256),
+                                      (17, 2048, 4304, 128)])
+@pytest.mark.parametrize('act', [ACT_NONE, ACT_GELU_TANH])
+def test_gemm_bf16_bias_act(m, n, k, bn, act):
+    torch.manual_seed(m + n)
+    a, b = rnd(m, k), rnd(n, k, std=0.02)
+    bias = torch.randn(n, device=DEV) * 0.1
+    out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(a, b, out, epilogue=EPI_BF16, bias=bias, act=act, block_n=bn)
+    ref = a.float() @ b.float().t() + bias
+    if act == ACT_GELU_TANH:
+        ref = torch.nn.functional.gelu(ref, approximate='tanh')
+    torch.cuda.synchronize()
+    close(out, ref)
+
+
+@pytest.mark.parametrize('tokens', [1, 50, 51, 64])
+@pytest.mark.parametrize('feat,k', [(1024, 1024), (2560, 1024), (32, 1024)])
+def test_gemm_swap_bf16(tokens, feat, k):
+    torch.manual_seed(tokens)
+    w, x = rnd(feat, k, std=0.02), rnd(tokens, k)
+    bias = torch.randn(feat, device=DEV) * 0.1
+    out = torch.empty(tokens, feat, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(w, x, out, epilogue=EPI_BF16, swap=True, bias=bias,
+             act=ACT_SILU)
+    ref = torch.nn.functional.silu(x.float() @ w.float().t() + bias)
+    torch.cuda.synchronize()
+    close(out, ref)
+
+
+@pytest.mark.parametrize('swap', [False, True])
+@pytest.mark.parametrize('split', [1, 4])
+def test_gemm_f32_acc_gate(swap, split):
+    torch.manual_seed(3)
+    T, F, K = (51, 1024, 4096) if swap else (816, 2048, 2048)
+    x, w = rnd(T, K), rnd(F, K, std=0.02)
+    res = torch.randn(T, F, device=DEV)
+    gate = torch.randn(F, device=DEV)
+    bias = torch.randn(F, device=DEV) * 0.1
+    out = res.clone()
+    if swap:
+        ops.gemm(w, x, out, epilogue=EPI_F32_ACC, swap=True, gate=gate,
+                 bias=bias, split_k=split, alpha=0.5)
+    else:
+        ops.gemm(x, w, out, epilogue=EPI_F32_ACC, gate=gate, bias=bias,
+                 split_k=split, alpha=0.5)
+    ref = res + 0.5 * gate * (x.float() @ w.float().t() + bias)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize('swap', [False, True])
+def test_gemm_f32_store_row_add(swap):
+    torch.manual_seed(4)
+    T, F, K = 768, 1152, 592
+    x, w = rnd(T, K), rnd(F, K, std=0.02)
+    pos = rnd(256, F, std=0.02)
+    bias = torch.randn(F, device=DEV) * 0.1
+    out = torch.empty(T, F, device=DEV)
+    if swap:
+        T = 50
+        x = x[:T].contiguous()
+        out = out[:T].contiguous()
+        ops.gemm(w, x, out, epilogue=EPI_F32_STORE, swap=True, bias=bias,
+                 row_add=pos, row_add_mod=256)
+    else:
+        ops.gemm(x, w, out, epilogue=EPI_F32_STORE, bias=bias, row_add=pos,
+                 row_add_mod=256)
+    ref = x.float() @ w.float().t() + bias + pos.float().repeat(3, 1)[:T]
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize('swap', [False, True])
+def test_gemm_geglu(swap):
+    torch.manual_seed(5)
+    T, F, K = (51, 4096, 1024) if swap else (816, 16384, 2048)
+    x = rnd(T, K)
+    g, u = rnd(F, K, std=0.02), rnd(F, K, std=0.02)
+    wp = pack_geglu(g, u)
+    out = torch.empty(T, F, device=DEV, dtype=torch.bfloat16)
+    if swap:
+        ops.gemm(wp, x, out, epilogue=EPI_GEGLU, swap=True)
+    else:
+        ops.gemm(x, wp, out, epilogue=EPI_GEGLU)
+    xf = x.float()
+    ref = torch.nn.functional.gelu(xf @ g.float().t(), approximate='tanh') * (
+        xf @ u.float().t())
+    torch.cuda.synchronize()
+    close(out, ref)
+
+
+def _rope_ref(x, pos, hd):
+    cs = rope_table(int(pos.max()) + 1, hd).to(x.device)
+    c = cs[pos.long(), :, 0].repeat(1, 2)[:, None]
+    s = cs[pos.long(), :, 1].repeat(1, 2)[:, None]
+    x1, x2 = x[..., :hd // 2], x[..., hd // 2:]
+    return x * c + torch.cat([-x2, x1], -1) * s
+
+
+@pytest.mark.parametrize('swap', [False, True])
+def test_gemm_qkv_rope(swap):
+    torch.manual_seed(6)
+    H, hd = 8, 256
+    T, K = (51, 1024) if swap else (816, 2048)
+    x = rnd(T, K)
+    qw, kw, vw = rnd(H * hd, K, std=0.02), rnd(hd, K, std=0.02), rnd(
+        hd, K, std=0.02)
+    wp = pack_qkv(qw, kw, vw, hd)
+    pos = (torch.arange(T, device=DEV) + (816 if swap else 0)).int()
+    cs = rope_table(1024, hd, device=DEV)
+    q = torch.empty(T, H * hd, device=DEV, dtype=torch.bfloat16)
+    kc = torch.zeros(T + 3, hd, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros(T + 3, hd, device=DEV, dtype=torch.bfloat16)
+    kw_ = dict(epilogue=EPI_QKV_ROPE, k_out=kc[2:], v_out=vc[2:], n_heads=H,
+               head_dim=hd, rope_cs=cs, positions=pos)
+    if swap:
+        ops.gemm(wp, x, q, swap=True, **kw_)
+    else:
+        ops.gemm(x, wp, q, **kw_)
+    xf = x.float()
+    qr = _rope_ref((xf @ qw.float().t()).view(T, H, hd), pos, hd)
+    kr = _rope_ref((xf @ kw.float().t()).view(T, 1, hd), pos, hd)
+    torch.cuda.synchronize()
+    close(q.view(T, H, hd), qr)
+    close(kc[2:2 + T], kr[:, 0])
+    close(vc[2:2 + T], xf @ vw.float().t())
+    assert kc[:2].abs().sum() == 0 and kc[2 + T:].abs().sum() == 0
+
+
+def _attn_ref(q, k, v, mask, scale):
+    # q [H, Sq, D], k/v [Skv, D], mask [Sq, Skv] bool
+    s = (q.float() @ k.float().t()) * scale
+    s = s.masked_fill(~mask[None], float('-inf'))
+    return torch.softmax(s, -1) @ v.float()
+
+
+@pytest.mark.parametrize('splits', [1, 7])
+def test_attention_suffix_mask_mqa(splits):
+    torch.manual_seed(7)
+    H, hd, E, S = 8, 256, 816, 51
+    q = rnd(S, H * hd)
+    kc, vc = rnd(E + S, hd), rnd(E + S, hd)
+    o = torch.empty(S, H * hd, device=DEV, dtype=torch.bfloat16)
+    valid = torch.ones(E, dtype=torch.uint8, device=DEV)
+    valid[800:] = 0
+    blk = torch.tensor([1, 2] + [2] * 49, dtype=torch.int32, device=DEV)
+    args = ops.attn_args(q, kc, vc, o, n_q=S, n_kv=E + S, heads=H, group=H,
+                         head_dim=hd, scale=hd ** -0.5, q_row_stride=H * hd,
+                         q_head_stride=hd, k_row_stride=hd, k_head_stride=0,
+                         v_row_stride=hd, v_head_stride=0,
+                         o_row_stride=H * hd, o_head_stride=hd,
+                         key_valid=valid, n_prefix=E, q_block=blk,
+                         k_block=blk, kv_splits=splits)
+    ws = torch.empty(max(ops.attention_workspace_bytes(args), 16),
+                     dtype=torch.uint8, device=DEV)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    ops.attention(args)
+    mask = torch.cat([valid.bool()[None].expand(S, E),
+                      blk[None, :] <= blk[:, None]], 1)
+    ref = _attn_ref(q.view(S, H, hd).transpose(0, 1), kc, vc, mask,
+                    hd ** -0.5)
+    torch.cuda.synchronize()
+    close(o.view(S, H, hd).transpose(0, 1), ref)
+
+
+def test_attention_prefix_bidirectional_and_causal():
+    torch.manual_seed(8)
+    H, hd, E = 8, 256, 816
+    q = rnd(E, H * hd)
+    kc, vc = rnd(E, hd), rnd(E, hd)
+    o = torch.empty_like(q)
+    valid = torch.ones(E, dtype=torch.uint8, device=DEV)
+    valid[790:] = 0
+    base = dict(n_q=E, n_kv=E, heads=H, group=H, head_dim=hd,
+                scale=hd ** -0.5, q_row_stride=H * hd, q_head_stride=hd,
+                k_row_stride=hd, k_head_stride=0, v_row_stride=hd,
+                v_head_stride=0, o_row_stride=H * hd, o_head_stride=hd)
+    ops.attention(ops.attn_args(q, kc, vc, o, key_valid=valid, **base))
+    ref = _attn_ref(q.view(E, H, hd).transpose(0, 1), kc, vc,
+                    valid.bool()[None].expand(E, E), hd ** -0.5)
+    torch.cuda.synchronize()
+    close(o.view(E, H, hd).transpose(0, 1), ref)
+    ar = torch.arange(E, dtype=torch.int32, device=DEV)
+    ops.attention(ops.attn_args(q, kc, vc, o, n_prefix=0, q_block=ar,
+                                k_block=ar, **base))
+    ref = _attn_ref(q.view(E, H, hd).transpose(0, 1), kc, vc,
+                    torch.ones(E, E, dtype=torch.bool, device=DEV).tril(),
+                    hd ** -0.5)
+    torch.cuda.synchronize()
+    close(o.view(E, H, hd).transpose(0, 1), ref)
+
+
+def test_attention_siglip_hd72_views():
+    torch.manual_seed(9)
+    V, P, H, hd = 3, 256, 16, 72
+    W = H * hd
+    qkv = rnd(V * P, 3 * W)
+    o = torch.empty(V * P, W, device=DEV, dtype=torch.bfloat16)
+    args = ops.attn_args(qkv, qkv[:, W:], qkv[:, 2 * W:], o, n_q=P, n_kv=P,
+                         heads=H, group=1, head_dim=hd, scale=hd ** -0.5,
+                         q_row_stride=3 * W, q_head_stride=hd,
+                         k_row_stride=3 * W, k_head_stride=hd,
+                         v_row_stride=3 * W, v_head_stride=hd,
+                         o_row_stride=W, o_head_stride=hd, batch=V,
+                         q_batch_rows=P, kv_batch_rows=P)
+    ops.attention(args)
+    x = qkv.float().view(V, P, 3, H, hd)
+    q, k, v = x[:, :, 0].transpose(1, 2), x[:, :, 1].transpose(1, 2), \
+        x[:, :, 2].transpose(1, 2)
+    ref = torch.softmax(q @ k.transpose(-1, -2) * hd ** -0.5, -1) @ v
+    torch.cuda.synchronize()
+    close(o.view(V, P, H, hd).transpose(1, 2), ref)
+
+
+@pytest.mark.parametrize('mode', [NORM_GEMMA_RMS, NORM_ADA_RMS, NORM_LAYER])
+@pytest.mark.parametrize('out_f32', [False, True])
+def test_norm(mode, out_f32):
+    torch.manual_seed(10)
+    R, D = 51, 1024
+    x = torch.randn(R, D, device=DEV) * 3 + 0.5
+    w = rnd(D, std=0.02) + (1 if mode == NORM_LAYER else 0)
+    b = rnd(D, std=0.02)
+    mod = torch.randn(2 * D, device=DEV) * 0.1
+    out = torch.empty(R, D, device=DEV,
+                      dtype=torch.float32 if out_f32 else torch.bfloat16)
+    ops.norm(mode, x, out, w=w, b=b, mod=mod, eps=1e-6)
+    if mode == NORM_LAYER:
+        ref = torch.nn.functional.layer_norm(x, (D,), w.float(), b.float(),
+                                             1e-6)
+    else:
+        n = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-6)
+        ref = n * (1 + w.float()) if mode == NORM_GEMMA_RMS else \
+            n * (1 + mod[:D]) + mod[D:]
+    torch.cuda.synchronize()
+    close(out, ref, 1e-2 if not out_f32 else 1e-5)
+
+
+def test_patchify_embed_small_linear():
+    torch.manual_seed(11)
+    img = torch.randint(0, 256, (3, 224, 224, 3), dtype=torch.uint8,
+                        device=DEV)
+    mean = torch.tensor([123.5, 116.0, 103.6], device=DEV)
+    std = torch.tensor([58.3, 57.0, 57.3], device=DEV)
+    out = torch.empty(768, 592, device=DEV, dtype=torch.bfloat16)
+    ops.patchify(img, 14, mean.tolist(), std.tolist(), out)
+    x = (img.float().permute(0, 3, 1, 2) - mean[:, None, None]) / (
+        std[:, None, None] + 1e-8)
+    ref = x.unfold(2, 14, 14).unfold(3, 14, 14)        # V,3,16,16,14,14
+    ref = ref.permute(0, 2, 3, 1, 4, 5).reshape(768, 588)
+    torch.cuda.synchronize()
+    close(out[:, :588], ref)
+    assert out[:, 588:].abs().sum() == 0
+
+    table = rnd(1000, 64, std=0.02)
+    ids = torch.randint(0, 1000, (7,), device=DEV)
+    e = torch.zeros(9, 64, device=DEV)
+    ops.embed_tokens(ids, table, 8.0, e[2:])
+    torch.cuda.synchronize()
+    torch.testing.assert_close(e[2:], table[ids].float() * 8.0)
+
+    x = torch.randn(50, 1024, device=DEV)
+    w = rnd(32, 1024, std=0.02)
+    bias = torch.randn(32, device=DEV)
+    acc = torch.randn(50, 32, device=DEV)
+    ref = acc - 0.1 * (x @ w.float().t() + bias)
+    ops.small_linear(x, w, acc, bias=bias, mode=2, alpha=-0.1)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(acc, ref, atol=1e-4, rtol=1e-4)
