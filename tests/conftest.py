@@ -10,6 +10,7 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line('markers', 'gpu: needs a CUDA device (B200)')
+    config.addinivalue_line('markers', 'slow: full-depth model cases')
 
 
 def pytest_collection_modifyitems(config, items):
