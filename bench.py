@@ -1,0 +1,411 @@
+"""Benchmark: PI0 batch-1 action-chunk latency and chunks/s on B200.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+                    [--workload pi0|pi05|loop]
+
+A "step" is one action chunk: one full PI0 inference (config[2]: 3 views
+224x224 uint8 -> SigLIP So400m -> Gemma-2B prefix prefill over 816 rows
+writing the bf16 KV cache -> 10 Euler steps of the 18-layer action expert
+over 51 suffix tokens), i.e. one replay of the engine's CUDA graph.
+Weights are seeded random bf16 of the real architecture (no checkpoint is
+available); inputs are seeded synthetic tensors of the benchmark's shapes.
+Every chunk streams ~6.6 GB of weights, far more than the 126 MB L2, so no L2
+flush is needed between timed iterations.
+
+N > 1 (torchrun): one independent replica per GPU (the path has no
+intra-request shard, so there is no collective on the data path); the
+barrier and the max-over-ranks reduction of the timings use NCCL.
+`value` = N * 1000 / (max-over-ranks ms per chunk).
+
+--impl reference times the reference algorithm's CPU path (the fp32 oracle
+port of the eager modules, all host threads) on a bounded sample and prints
+the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = ('PI0 batch-1 action-chunk latency (ms) and chunks/s at 1/2/4/8 '
+          'B200; roofline %')
+PEAKS_FALLBACK = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0,
+                  'bf16_tflops_sustained': 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), 'measured'
+    return PEAKS_FALLBACK, 'fallback'
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    Q = ('index,clocks.sm,clocks.max.sm,power.draw,'
+         'clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+         'clocks_event_reasons.hw_thermal_slowdown,'
+         'clocks_event_reasons.sw_thermal_slowdown,'
+         'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--query-gpu={self.Q}',
+                 '--format=csv,noheader,nounits', '-i', str(self.idx),
+                 '-lms', '200'], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None,
+                    'reasons': ['unsampled']}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
+                 'sw_power_cap']
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == 'active':
+                    reasons.add(n)
+        return {'sm_mhz': statistics.median(sm) if sm else None,
+                'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU reference arm (oracle port of the eager reference, all host threads)
+# ---------------------------------------------------------------------------
+
+def cpu_chunk_sample(threads: int, repeats: int = 1):
+    """Time one SigLIP layer (3 views incl. patch embed / post-LN), one
+    Gemma-2B prefix layer (816 rows, bidirectional) and one expert layer
+    step (51 suffix rows over 816 cached keys, incl. suffix embedding and
+    action head) with the fp32 oracle; scale to a full chunk as
+    27*vision + 17.05*prefix + 10*18*expert (the last prefix layer only
+    computes its K/V: 0.05 of a layer).  Returns (ms per chunk, detail)."""
+    from fluxvla_b200.config import PI0Config
+    from fluxvla_b200.weights import make_weights_matching
+    from oracle import pi0_oracle as O
+    torch.set_num_threads(threads)
+    cfg = PI0Config(vis_layers=1, llm_layers=1, exp_layers=1)
+    W = make_weights_matching(cfg, 0, lambda n: n != 'llm.embed')
+    g = torch.Generator().manual_seed(0)
+    pix = torch.randn(3, 3, 224, 224, generator=g)
+    x = torch.randn(1, 816, 2048, generator=g)
+    kv = [(torch.randn(1, 1, 816, 256, generator=g),
+           torch.randn(1, 1, 816, 256, generator=g))]
+    state = torch.randn(1, 32, generator=g)
+    xt = torch.randn(1, 50, 32, generator=g)
+    pad = torch.ones(1, 816, dtype=torch.bool)
+    pos = torch.arange(816)[None]
+    cos, sin = O.rope_cos_sin(pos, 256)
+    mask = O.additive_mask(torch.ones(1, 816, 816, dtype=torch.bool))
+
+    def vis():
+        O.siglip_forward(pix, W, 1, cfg.vis_heads)
+
+    def llm():
+        O.gemma_layer(x, W, 'llm.l0.', cos, sin, mask, 8, 1, 256)
+
+    def exp():
+        O.denoise_step(cfg, W, state, pad, kv, xt, torch.ones(1), 1)
+
+    with torch.no_grad():
+        for f in (vis, llm, exp):
+            f()  # warm-up
+        res = {}
+        for name, f in (('vision_layer', vis), ('prefix_layer', llm),
+                        ('expert_layer_step', exp)):
+            ts = []
+            for _ in range(max(1, repeats)):
+                t0 = time.perf_counter()
+                f()
+                ts.append(time.perf_counter() - t0)
+            res[name] = statistics.median(ts) * 1e3
+    ms = 27 * res['vision_layer'] + 17.05 * res['prefix_layer'] + \
+        180 * res['expert_layer_step']
+    return ms, res
+
+
+SAMPLE_DOC = ('one SigLIP layer (3 views), one Gemma-2B prefix layer (816 '
+              'rows) and one expert layer step (51 rows, 816 cached keys) of '
+              'the fp32 oracle port, scaled to a chunk as 27*vision + '
+              '17.05*prefix + 180*expert; ms: ')
+
+
+def workload_name(w):
+    return {
+        'pi0': 'config[2]: PI0 batch-1 full inference, 3 views 224x224 uint8, '
+               '48 prompt tokens, 816-row prefix, state + 50 action tokens, '
+               '10 Euler steps',
+        'pi05': 'config[3]: PI0.5 batch-1 full inference, 3 views, 80 prompt '
+                'tokens (48 text + 32 state), 848-row prefix, 50 action '
+                'tokens, adaRMS expert, 10 Euler steps',
+        'loop': 'config[1]: PI0 action-expert loop only, 816-row prefix KV '
+                'cache, 51 suffix tokens, 10 Euler steps',
+    }[w]
+
+
+def run_reference(args):
+    if int(os.environ.get('RANK', '0')) != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    ms_list, detail = [], None
+    for i in range(args.warmup + args.steps):
+        ms, detail = cpu_chunk_sample(threads)
+        if i >= args.warmup:
+            ms_list.append(ms)
+    ms = statistics.median(ms_list)
+    v = 1000.0 / ms
+    sample = 'per step: ' + SAMPLE_DOC + json.dumps(
+        {k: round(x, 2) for k, x in detail.items()})
+    line = {'metric': METRIC, 'value': v, 'unit': 'chunks/s',
+            'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+            'impl': 'reference',
+            'config': {'workload': workload_name(args.workload),
+                       'parallelism': f'replicas{args.gpus}'},
+            'cpu_baseline': {'value': v, 'unit': 'chunks/s', 'cores': threads,
+                             'kind': 'port', 'sample': sample},
+            'e2e': {'value': v, 'unit': 'chunks/s', 'h2d_bytes_per_step': 0,
+                    'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    from fluxvla_b200 import ops
+    from fluxvla_b200._lib import EPI_GEGLU
+    from fluxvla_b200.config import PI0Config, pi05_config
+    from fluxvla_b200.engine import PI0EngineB200
+    from fluxvla_b200.weights import make_weights
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        dist.init_process_group('nccl', device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    w = args.workload
+    cfg = pi05_config() if w == 'pi05' else PI0Config()
+    n_tok = 80 if w == 'pi05' else 48
+    E = cfg.n_views * cfg.tokens_per_view + n_tok
+    parts = ('exp', 'heads') if w == 'loop' else ('vision', 'llm', 'exp',
+                                                  'heads')
+    W = make_weights(cfg, seed=0, parts=parts, device=dev)
+    eng = PI0EngineB200(cfg, W, prefix_len=E, device=dev)
+    del W
+    torch.cuda.empty_cache()
+
+    g = torch.Generator().manual_seed(1 + rank)
+    imgs = torch.randint(0, 256, (cfg.n_views, 224, 224, 3), generator=g,
+                         dtype=torch.uint8).pin_memory()
+    toks = torch.randint(0, cfg.vocab, (1, n_tok), generator=g).pin_memory()
+    state = torch.randn(1, cfg.state_dim, generator=g).pin_memory()
+    noise = torch.randn(1, cfg.n_actions, cfg.action_dim,
+                        generator=g).pin_memory()
+    if w == 'loop':
+        kc = torch.randn(cfg.exp_layers, E, cfg.head_dim, generator=g)
+        vc = torch.randn(cfg.exp_layers, E, cfg.head_dim, generator=g)
+        eng.set_prefix_cache(kc.to(dev, torch.bfloat16),
+                             vc.to(dev, torch.bfloat16))
+
+        def call():
+            eng.load_inputs(state=state, noise=noise)
+            if eng.graph is None:
+                eng.capture(prefix=False)
+            eng.replay()
+            return eng.actions.to('cpu')
+        h2d = state.numel() * 4 + noise.numel() * 4
+    else:
+        def call():
+            return eng.predict_action(imgs, toks, state, noise=noise)
+        h2d = (imgs.numel() + toks.numel() * 8 + state.numel() * 4 +
+               noise.numel() * 4 + E * (1 + 4) + eng.S * 4)
+    d2h = cfg.n_actions * cfg.action_dim * 4
+
+    call()  # capture + first run
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        eng.replay()
+    torch.cuda.synchronize(dev)
+
+    # ---- device-timed region: K graph replays (inputs resident) ----
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.6)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    # ---- end-to-end through predict_action (pinned H2D + D2H per chunk) --
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = call()
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps)
+    barrier()
+    assert torch.isfinite(out).all()
+
+    # ---- roofline: dominant kernel timed alone with CUDA events ----
+    peaks, peak_kind = load_peaks()
+    if w != 'loop':
+        P, B = eng.P, eng.B
+        reps, L = 3, cfg.llm_layers - 1
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record(stream)
+        for _ in range(reps):
+            for i in range(L):
+                ops.gemm(B['l_xn'], P[f'llm.l{i}.gu'], B['l_h'],
+                         epilogue=EPI_GEGLU, block_n=256)
+        ev[1].record(stream)
+        torch.cuda.synchronize(dev)
+        t_launch = ev[0].elapsed_time(ev[1]) / (reps * L) * 1e-3
+        flops = 2.0 * E * cfg.llm_width * 2 * cfg.llm_mlp
+        ach = flops / t_launch / 1e12
+        roof = {'kernel': 'gemm_tc_kernel<256,4> Gemma-2B gate/up GeGLU '
+                          f'[{E}x2048]x[32768x2048]^T',
+                'bound': 'tensor', 'achieved': ach,
+                'peak': peaks['bf16_tflops'], 'unit': 'TFLOP/s',
+                'frac': ach / peaks['bf16_tflops'],
+                'peak_source': f'{peak_kind} burst bf16 (kernel timed alone)',
+                'traffic': None, 'launch_us': t_launch * 1e6}
+    else:
+        wbytes = sum(v.numel() * v.element_size() for k, v in eng.P.items()
+                     if k.startswith('exp.'))
+        kvb = 2 * cfg.exp_layers * E * cfg.head_dim * 2
+        ach = (wbytes + kvb) * len(eng.times) / (ms * 1e-3) / 1e9
+        roof = {'kernel': 'denoise chunk (all loop kernels)', 'bound': 'hbm',
+                'achieved': ach, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
+                'frac': ach / peaks['hbm_gbs'],
+                'peak_source': f'{peak_kind} HBM copy', 'traffic': None}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        cms, detail = cpu_chunk_sample(threads, repeats=3)
+        cpu = {'value': 1000.0 / cms, 'unit': 'chunks/s', 'cores': threads,
+               'kind': 'port',
+               'sample': SAMPLE_DOC + json.dumps(
+                   {k: round(x, 2) for k, x in detail.items()}),
+               'ms_per_chunk': cms}
+
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': world * 1000.0 / ms,
+            'unit': 'chunks/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'bf16',
+            'data': 'synthetic (seeded random bf16 weights of the real '
+                    'architecture, seeded inputs)',
+            'config': {'workload': workload_name(w), 'batch_per_gpu': 1,
+                       'prefix_rows': E, 'suffix_rows': eng.S,
+                       'euler_steps': len(eng.times),
+                       'parallelism': f'replicas{world}',
+                       'l2': 'no flush: every chunk streams ~6.6 GB of '
+                             'weights (> 126 MB L2)'},
+            'latency_ms': ms,
+            'e2e': {'value': world * 1000.0 / e2e_ms, 'unit': 'chunks/s',
+                    'latency_ms': e2e_ms, 'h2d_bytes_per_step': int(h2d),
+                    'd2h_bytes_per_step': int(d2h)},
+            'roofline': roof, 'cpu_baseline': cpu,
+            'gpu_launches': int(eng.launches_per_call * args.steps),
+            'launches_per_chunk': eng.launches_per_call,
+            'clocks': clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    ap.add_argument('--workload', default='pi0',
+                    choices=['pi0', 'pi05', 'loop'])
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == 'reference':
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == '__main__':
+    sys.exit(main())

@@ -129,3 +129,13 @@ def make_weights(cfg: PI0Config, seed: int = 0,
                  device='cpu') -> Dict[str, torch.Tensor]:
     return {n: gen_tensor(n, s, i, seed, device)
             for n, s, i in weight_shapes(cfg, parts)}
+
+
+def make_weights_matching(cfg: PI0Config, seed: int, predicate,
+                          parts: Iterable[str] = ('vision', 'llm', 'exp',
+                                                  'heads'),
+                          device='cpu') -> Dict[str, torch.Tensor]:
+    """Only the tensors whose name satisfies ``predicate`` (same values as
+    make_weights would give them)."""
+    return {n: gen_tensor(n, s, i, seed, device)
+            for n, s, i in weight_shapes(cfg, parts) if predicate(n)}
