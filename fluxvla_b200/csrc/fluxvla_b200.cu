@@ -344,3 +344,93 @@ int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free attention.
+//
+// Some callers cannot allocate device memory at all: an embedded robot
+// controller whose memory budget is fixed at start-up, a process running
+// under an allocator that forbids cudaMalloc after initialisation, or a
+// foreign-language binding that has no way to hand us a device buffer.
+// fvb_attention_noalloc serves them: the split-over-keys partial results
+// live in the file-scope array below instead of a caller workspace.  Every
+// GPU that loads this library reserves FVB_NOALLOC_SCRATCH_BYTES for it until
+// the process exits.  All calls on a device share the one array; it keeps
+// the last call's contents.  Nothing in it has to start at zero: every split
+// writes all of its partial rows (empty key ranges write m = -inf, l = 0)
+// before the combine reads them.  Calls whose kernels overlap on the GPU
+// (different streams, or concurrent host threads) race on the array.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char
+    g_noalloc_scratch[FVB_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch for the current device.  In host code
+// the symbol name is only a host-side stand-in, so the address is looked up
+// once per device (with that device current) and cached.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* ptrs[128] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "fvb_attention_noalloc: cudaGetDevice: %s",
+                cudaGetErrorString(e));
+  if (dev < 0 || dev >= 128)
+    return fail(FVB_ERR_UNSUPPORTED, "fvb_attention_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(FVB_ERR_CUDA,
+                  "fvb_attention_noalloc: cudaGetSymbolAddress: %s",
+                  cudaGetErrorString(e));
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return FVB_OK;
+}
+
+extern "C" int fvb_attention_noalloc(const fvb_attn_args* a, void* stream) {
+  fvb::AttnDev d;
+  int r = attn_prepare(a, &d);
+  if (r) return r;
+  const long long rows = (long long)a->batch * a->heads * a->n_q;
+  const long long need =
+      d.splits > 1 ? (long long)d.splits * rows * (a->head_dim + 2) * 4 : 0;
+  if (need > (long long)FVB_NOALLOC_SCRATCH_BYTES)
+    return fail(FVB_ERR_WORKSPACE,
+                "fvb_attention_noalloc: %d key splits x %lld query rows need "
+                "%lld bytes of scratch, more than the %lld-byte limit; use "
+                "fewer kv_splits or fvb_attention with a caller workspace",
+                d.splits, rows, need, (long long)FVB_NOALLOC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  if (d.splits > 1) {
+    r = noalloc_scratch(&ws);
+    if (r) return r;
+  }
+  d.part_o = (float*)ws;
+  d.part_ml = ws ? d.part_o + (long long)d.splits * rows * a->head_dim
+                 : nullptr;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid((a->n_q + fvb::ATT_BM - 1) / fvb::ATT_BM, a->heads,
+            a->batch * d.splits);
+  if (a->head_dim == 256) {
+    constexpr int S = fvb::attn_smem_bytes<256, 256>();
+    cudaFuncSetAttribute(fvb::attn_kernel<256, 256>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, S);
+    fvb::attn_kernel<256, 256><<<grid, fvb::ATT_THREADS, S, st>>>(d);
+  } else {
+    constexpr int S = fvb::attn_smem_bytes<72, 80>();
+    cudaFuncSetAttribute(fvb::attn_kernel<72, 80>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, S);
+    fvb::attn_kernel<72, 80><<<grid, fvb::ATT_THREADS, S, st>>>(d);
+  }
+  r = check_launch("fvb_attention_noalloc");
+  if (r || d.splits == 1) return r;
+  if (a->head_dim == 256)
+    fvb::attn_combine_kernel<256><<<(unsigned)rows, 256, 0, st>>>(d);
+  else
+    fvb::attn_combine_kernel<72><<<(unsigned)rows, 96, 0, st>>>(d);
+  return check_launch("fvb_attention_noalloc (combine)");
+}

@@ -139,6 +139,24 @@ int64_t fvb_attention_workspace_bytes(const fvb_attn_args* args);
 /* Merge of the kv_splits partial results into args->o. */
 int fvb_attention_combine(const fvb_attn_args* args, void* stream);
 
+/* Size of the library-owned scratch array used by fvb_attention_noalloc. */
+#define FVB_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* fvb_attention (plus its combine) without a caller workspace.  This entry
+ * point has no counterpart in the reference; it exists for callers that
+ * cannot allocate device memory (fixed memory budgets on embedded robot
+ * controllers, allocators that forbid cudaMalloc after start-up, bindings
+ * with no way to pass a device buffer).  The split partials go to a
+ * file-scope device array of FVB_NOALLOC_SCRATCH_BYTES (8 MiB) that every
+ * GPU loading the library holds until exit; args->workspace is ignored.
+ * Calls needing more scratch than that fail with FVB_ERR_WORKSPACE.  The
+ * first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  It allocates nothing.  All calls share the array and it keeps the
+ * last call's contents (nothing in it needs clearing); calls that overlap on
+ * the GPU race on it.                                                      */
+int fvb_attention_noalloc(const fvb_attn_args* args, void* stream);
+
 /* Row normalisation, f32 input rows [rows, dim] (row stride ld_in), output
  * bf16 or f32 (out_f32 != 0) with row stride ld_out.
  * mode FVB_NORM_GEMMA_RMS: w = bf16 [dim]; FVB_NORM_ADA_RMS: mod = f32
