@@ -288,6 +288,14 @@ def run_b200(args):
     for _ in range(args.warmup):
         eng.replay()
     torch.cuda.synchronize(dev)
+    if args.profile:
+        # one graph replay bracketed for `ncu --profile-from-start off`
+        torch.cuda.cudart().cudaProfilerStart()
+        eng.replay()
+        torch.cuda.synchronize(dev)
+        torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps({'profiled_launches': eng.launches_per_call}))
+        return 0
 
     # ---- device-timed region: K graph replays (inputs resident) ----
     sampler = ClockSampler(local) if rank == 0 else None
@@ -400,6 +408,9 @@ def main():
     ap.add_argument('--workload', default='pi0',
                     choices=['pi0', 'pi05', 'loop'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--profile', action='store_true',
+                    help='replay one chunk between cudaProfilerStart/Stop '
+                         'and exit (for ncu --profile-from-start off)')
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == 'reference':
