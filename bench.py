@@ -245,7 +245,10 @@ def run_b200(args):
         return float(t.item())
 
     w = args.workload
-    cfg = pi05_config() if w == 'pi05' else PI0Config()
+    depth = {} if not args.depth else dict(
+        vis_layers=args.depth, llm_layers=args.depth, exp_layers=args.depth,
+        vocab=4096)
+    cfg = pi05_config(**depth) if w == 'pi05' else PI0Config(**depth)
     n_tok = 80 if w == 'pi05' else 48
     E = cfg.n_views * cfg.tokens_per_view + n_tok
     parts = ('exp', 'heads') if w == 'loop' else ('vision', 'llm', 'exp',
@@ -408,6 +411,8 @@ def main():
     ap.add_argument('--workload', default='pi0',
                     choices=['pi0', 'pi05', 'loop'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--depth', type=int, default=0,
+                    help='profiling only: layers per tower (0 = full model)')
     ap.add_argument('--profile', action='store_true',
                     help='replay one chunk between cudaProfilerStart/Stop '
                          'and exit (for ncu --profile-from-start off)')
