@@ -69,6 +69,8 @@ EXPORTS = {
                                    C.c_int32, C.c_void_p, C.c_int32,
                                    C.c_int32, C.c_float, C.c_void_p,
                                    C.c_int64, C.c_void_p]),
+    'fvb_gemm_trace_next': (C.c_int, []),
+    'fvb_gemm_trace_read': (C.c_int, [C.c_void_p, C.c_int32]),
     'fvb_get_device_status': (C.c_int, [C.POINTER(C.c_int), C.c_int]),
     'fvb_last_error': (C.c_char_p, []),
     'fvb_version': (C.c_int, []),

@@ -110,6 +110,8 @@ __global__ void __launch_bounds__(ATT_THREADS)
   uint8_t* sMask = reinterpret_cast<uint8_t*>(sV + 2 * TILE);  // [2][64]
   int* sKb = reinterpret_cast<int*>(sMask + 128);              // [2][64]
 
+  griddep_wait();
+  griddep_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = blockIdx.x * ATT_BM;
   const int h = blockIdx.y;
@@ -327,6 +329,8 @@ __global__ void __launch_bounds__(ATT_THREADS)
 // One CTA per (batch*head, query row); HD threads max 256.
 template <int HD>
 __global__ void attn_combine_kernel(const AttnDev p) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x;  // over batch*heads*n_q
   const int d = threadIdx.x;
   const long long rows = (long long)p.batch * p.heads * p.n_q;

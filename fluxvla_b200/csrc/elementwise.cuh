@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(NORM_THREADS)
                 const bf16* __restrict__ b, const float* __restrict__ mod,
                 float eps) {
   __shared__ float red[32];
+  griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x;
   const float* xr = x + (long long)row * ld_in;
   float s = 0.f, ss = 0.f;
@@ -82,6 +84,8 @@ __global__ void patchify_kernel(const uint8_t* __restrict__ img, int H, int W,
                                 int P, float m0, float m1, float m2, float s0,
                                 float s1, float s2, bf16* __restrict__ out,
                                 long long ldo) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int gw = W / P, gh = H / P;
   const int r = blockIdx.x;
   const int v = r / (gh * gw), py = (r / gw) % gh, px = r % gw;
@@ -105,6 +109,8 @@ __global__ void embed_kernel(const long long* __restrict__ ids,
                              const bf16* __restrict__ table, int dim,
                              float scale, float* __restrict__ out,
                              long long ldo) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long id = ids[blockIdx.x];
   const bf16* src = table + id * dim;
   float* dst = out + (long long)blockIdx.x * ldo;
@@ -119,6 +125,8 @@ __global__ void small_linear_kernel(const float* __restrict__ x, long long ldx,
                                     const float* __restrict__ bias, int act,
                                     int mode, float alpha, void* out,
                                     long long ldo) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= T * N) return;

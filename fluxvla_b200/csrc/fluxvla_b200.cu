@@ -75,11 +75,55 @@ int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t k,
   return FVB_OK;
 }
 
-template <int BN>
+// Programmatic dependent launch is on unless FVB_PDL=0: each kernel may
+// start its prologue (and the GEMMs their weight prefetch) while the
+// previous kernel in the stream drains; every kernel executes
+// griddepcontrol.wait before touching data produced upstream.
+bool pdl_enabled() {
+  static const int v = [] {
+    const char* e = getenv("FVB_PDL");
+    return e ? atoi(e) : 1;
+  }();
+  return v != 0;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block,
+             size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "%s: launch failed: %s", what,
+                cudaGetErrorString(e));
+  return check_launch(what);
+}
+
+int sm_count() {
+  static int counts[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = n > 0 ? n : 148;
+  }
+  return counts[dev];
+}
+
+template <int BN, int EPI, bool SWAP, int ACT = FVB_ACT_NONE>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
-                const fvb::GemmDev& d, dim3 grid, cudaStream_t st) {
+                const fvb::GemmDev& d, cudaStream_t st) {
   using C = fvb::GemmCfg<BN>;
-  auto kern = fvb::gemm_tc_kernel<BN, C::STAGES>;
+  auto kern = fvb::gemm_tc_kernel<BN, C::STAGES, EPI, SWAP, ACT>;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -88,9 +132,12 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
                   cudaGetErrorString(cudaGetLastError()));
     attr = true;
   }
-  kern<<<grid, fvb::GEMM_THREADS, C::SMEM, st>>>(ma, mb, d);
-  return check_launch("fvb_gemm");
+  const int grid = d.n_work < sm_count() ? d.n_work : sm_count();
+  return launch_k("fvb_gemm", kern, dim3(grid), dim3(fvb::GEMM_THREADS),
+                  (size_t)C::SMEM, st, ma, mb, d);
 }
+
+int g_trace_next = 0;
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -113,6 +160,22 @@ int fvb_get_device_status(int* status, int reset) {
     if (e != cudaSuccess)
       return fail(FVB_ERR_CUDA, "reset status: %s", cudaGetErrorString(e));
   }
+  return FVB_OK;
+}
+
+int fvb_gemm_trace_next(void) {
+  g_trace_next = 1;
+  return FVB_OK;
+}
+
+int fvb_gemm_trace_read(uint64_t* host_out, int32_t max_ctas) {
+  if (!host_out || max_ctas <= 0)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm_trace_read: bad arguments");
+  const int n = max_ctas < fvb::GEMM_TRACE_CTAS ? max_ctas : fvb::GEMM_TRACE_CTAS;
+  cudaError_t e = cudaMemcpyFromSymbol(host_out, fvb::g_gemm_trace,
+                                       (size_t)n * 16 * sizeof(uint64_t));
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
   return FVB_OK;
 }
 
@@ -153,6 +216,16 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
 
   int bn = a->block_n;
   if (bn == 0) bn = a->swap ? 64 : 128;
+  if (a->swap) {
+    if (a->block_n != 0 && a->block_n != 64)
+      return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: swap uses block_n 64");
+    bn = 64;
+  } else if (!aligned16(a->out) ||
+             ((a->epilogue == FVB_EPI_QKV_ROPE) && (a->n % 32 || a->head_dim % 32))) {
+    return fail(FVB_ERR_INVALID_ARG,
+                "fvb_gemm: output must be 16B aligned (QKV: n, head_dim "
+                "multiples of 32)");
+  }
   if (bn != 64 && bn != 128 && bn != 256)
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: block_n must be 64/128/256");
 
@@ -164,7 +237,7 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
 
   fvb::GemmDev d;
   d.m = a->m; d.n = a->n; d.k = a->k;
-  d.swap = a->swap; d.epi = a->epilogue; d.act = a->act;
+  d.act = a->act;
   d.k_tiles = (a->k + fvb::GEMM_BK - 1) / fvb::GEMM_BK;
   d.kt_per_split = (d.k_tiles + split - 1) / split;
   d.split = (d.k_tiles + d.kt_per_split - 1) / d.kt_per_split;
@@ -176,13 +249,31 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   d.v_out = reinterpret_cast<bf16*>(a->v_out);
   d.ld_kv = a->ld_kv; d.n_heads = a->n_heads; d.head_dim = a->head_dim;
   d.rope_cs = a->rope_cs; d.positions = a->positions;
+  d.trace = g_trace_next ? 1 : 0;
+  g_trace_next = 0;
 
-  dim3 grid((a->m + fvb::GEMM_BM - 1) / fvb::GEMM_BM, (a->n + bn - 1) / bn,
-            d.split);
+  d.m_tiles = (a->m + fvb::GEMM_BM - 1) / fvb::GEMM_BM;
+  d.n_tiles = (a->n + bn - 1) / bn;
+  d.n_work = d.m_tiles * d.n_tiles * d.split;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (bn == 64) return launch_gemm<64>(ma, mb, d, grid, st);
-  if (bn == 128) return launch_gemm<128>(ma, mb, d, grid, st);
-  return launch_gemm<256>(ma, mb, d, grid, st);
+#define FVB_EPI_CASES(BN, SWAP)                                            \
+  switch (a->epilogue) {                                                   \
+    case FVB_EPI_BF16:                                                     \
+      if (a->act == FVB_ACT_GELU_TANH)                                     \
+        return launch_gemm<BN, FVB_EPI_BF16, SWAP, FVB_ACT_GELU_TANH>(ma, mb, d, st); \
+      if (a->act == FVB_ACT_SILU)                                          \
+        return launch_gemm<BN, FVB_EPI_BF16, SWAP, FVB_ACT_SILU>(ma, mb, d, st); \
+      return launch_gemm<BN, FVB_EPI_BF16, SWAP>(ma, mb, d, st);           \
+    case FVB_EPI_F32_STORE: return launch_gemm<BN, FVB_EPI_F32_STORE, SWAP>(ma, mb, d, st); \
+    case FVB_EPI_F32_ACC: return launch_gemm<BN, FVB_EPI_F32_ACC, SWAP>(ma, mb, d, st); \
+    case FVB_EPI_GEGLU: return launch_gemm<BN, FVB_EPI_GEGLU, SWAP>(ma, mb, d, st); \
+    default: return launch_gemm<BN, FVB_EPI_QKV_ROPE, SWAP>(ma, mb, d, st); \
+  }
+  if (a->swap) FVB_EPI_CASES(64, true)
+  if (bn == 64) FVB_EPI_CASES(64, false)
+  if (bn == 128) FVB_EPI_CASES(128, false)
+  FVB_EPI_CASES(256, false)
+#undef FVB_EPI_CASES
 }
 
 static int attn_prepare(const fvb_attn_args* a, fvb::AttnDev* d) {
@@ -254,7 +345,8 @@ int fvb_attention(const fvb_attn_args* a, void* stream) {
                            cudaFuncAttributeMaxDynamicSharedMemorySize, S);
       attr = true;
     }
-    fvb::attn_kernel<256, 256><<<grid, fvb::ATT_THREADS, S, st>>>(d);
+    return launch_k("fvb_attention", fvb::attn_kernel<256, 256>, grid,
+                    dim3(fvb::ATT_THREADS), (size_t)S, st, d);
   } else {
     constexpr int S = fvb::attn_smem_bytes<72, 80>();
     static bool attr = false;
@@ -263,9 +355,9 @@ int fvb_attention(const fvb_attn_args* a, void* stream) {
                            cudaFuncAttributeMaxDynamicSharedMemorySize, S);
       attr = true;
     }
-    fvb::attn_kernel<72, 80><<<grid, fvb::ATT_THREADS, S, st>>>(d);
+    return launch_k("fvb_attention", fvb::attn_kernel<72, 80>, grid,
+                    dim3(fvb::ATT_THREADS), (size_t)S, st, d);
   }
-  return check_launch("fvb_attention");
 }
 
 int fvb_attention_combine(const fvb_attn_args* a, void* stream) {
@@ -277,10 +369,10 @@ int fvb_attention_combine(const fvb_attn_args* a, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int rows = a->batch * a->heads * a->n_q;
   if (a->head_dim == 256)
-    fvb::attn_combine_kernel<256><<<rows, 256, 0, st>>>(d);
-  else
-    fvb::attn_combine_kernel<72><<<rows, 96, 0, st>>>(d);
-  return check_launch("fvb_attention_combine");
+    return launch_k("fvb_attention_combine", fvb::attn_combine_kernel<256>,
+                    dim3(rows), dim3(256), 0, st, d);
+  return launch_k("fvb_attention_combine", fvb::attn_combine_kernel<72>,
+                  dim3(rows), dim3(96), 0, st, d);
 }
 
 int fvb_norm(int32_t mode, const float* x, int64_t ld_in, void* out,
@@ -298,11 +390,11 @@ int fvb_norm(int32_t mode, const float* x, int64_t ld_in, void* out,
     return fail(FVB_ERR_INVALID_ARG, "fvb_norm: weight and bias required");
   if (mode < 0 || mode > 2)
     return fail(FVB_ERR_INVALID_ARG, "fvb_norm: bad mode");
-  fvb::norm_kernel<<<rows, fvb::NORM_THREADS, 0,
-                     reinterpret_cast<cudaStream_t>(stream)>>>(
-      mode, x, ld_in, out, ld_out, out_f32, dim, (const bf16*)w,
-      (const bf16*)b, mod, eps);
-  return check_launch("fvb_norm");
+  return launch_k("fvb_norm", fvb::norm_kernel, dim3(rows),
+                  dim3(fvb::NORM_THREADS), 0,
+                  reinterpret_cast<cudaStream_t>(stream), (int)mode, x,
+                  (long long)ld_in, out, (long long)ld_out, (int)out_f32,
+                  (int)dim, (const bf16*)w, (const bf16*)b, mod, eps);
 }
 
 int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
@@ -312,10 +404,11 @@ int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
       height % patch || width % patch || ldo < 3 * patch * patch)
     return fail(FVB_ERR_INVALID_ARG, "fvb_patchify: bad arguments");
   const int rows = views * (height / patch) * (width / patch);
-  fvb::patchify_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      images, height, width, patch, mean3[0], mean3[1], mean3[2], std3[0],
-      std3[1], std3[2], (bf16*)out, ldo);
-  return check_launch("fvb_patchify");
+  return launch_k("fvb_patchify", fvb::patchify_kernel, dim3(rows), dim3(256),
+                  0, reinterpret_cast<cudaStream_t>(stream), images,
+                  (int)height, (int)width, (int)patch, mean3[0], mean3[1],
+                  mean3[2], std3[0], std3[1], std3[2], (bf16*)out,
+                  (long long)ldo);
 }
 
 int fvb_embed_tokens(const int64_t* ids, int32_t n, const void* table,
@@ -323,9 +416,10 @@ int fvb_embed_tokens(const int64_t* ids, int32_t n, const void* table,
                      void* stream) {
   if (!ids || !table || !out || n <= 0 || dim <= 0)
     return fail(FVB_ERR_INVALID_ARG, "fvb_embed_tokens: bad arguments");
-  fvb::embed_kernel<<<n, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      (const long long*)ids, (const bf16*)table, dim, scale, out, ldo);
-  return check_launch("fvb_embed_tokens");
+  return launch_k("fvb_embed_tokens", fvb::embed_kernel, dim3(n), dim3(256),
+                  0, reinterpret_cast<cudaStream_t>(stream),
+                  (const long long*)ids, (const bf16*)table, (int)dim, scale,
+                  out, (long long)ldo);
 }
 
 int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
@@ -337,10 +431,11 @@ int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
   const long long warps = (long long)t * n;
   const int threads = 256;
   const long long blocks = (warps * 32 + threads - 1) / threads;
-  fvb::small_linear_kernel<<<(unsigned)blocks, threads, 0,
-                             reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, ldx, t, k, (const bf16*)w, ldw, n, bias, act, mode, alpha, out, ldo);
-  return check_launch("fvb_small_linear");
+  return launch_k("fvb_small_linear", fvb::small_linear_kernel,
+                  dim3((unsigned)blocks), dim3(threads), 0,
+                  reinterpret_cast<cudaStream_t>(stream), x, (long long)ldx,
+                  (int)t, (int)k, (const bf16*)w, (long long)ldw, (int)n, bias,
+                  (int)act, (int)mode, alpha, out, (long long)ldo);
 }
 
 }  // extern "C"

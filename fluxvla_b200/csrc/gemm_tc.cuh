@@ -1,18 +1,33 @@
 // tcgen05 / TMEM tensor-core GEMM for sm_100a:  C[M,N] = A[M,K] * B[N,K]^T.
 //
-// One CTA computes one 128 x BN output tile:
+// Persistent: one CTA per SM walks the 128 x BN output tiles (and K splits)
+// with a grid-stride loop; tile index = m-tile fastest, so the CTAs running
+// at the same time share the same B (weight) tile in the normal orientation
+// and stream consecutive weight tiles in the swapped one.
 //   warp 0 (one lane)  : TMA producer, STAGES-deep ring of (A,B) k-tiles
 //                        (64 bf16 = 128 B per row, 128-byte swizzle)
-//   warp 1             : allocates BN TMEM columns; one lane issues
-//                        tcgen05.mma (M=128, N=BN, K=16) x4 per k-tile and
-//                        commits each stage back to the producer
+//   warp 1             : allocates 2*BN TMEM columns (two accumulators); one
+//                        lane issues tcgen05.mma (M=128, N=BN, K=16) x4 per
+//                        k-tile and commits stages back to the producer
 //   warps 2..5         : epilogue; warp w reads TMEM lanes 32*(w%4)..+31
-//                        (one accumulator row per thread) with tcgen05.ld
-//                        and applies the fused epilogue.
+//                        (one accumulator row per thread) with tcgen05.ld.
+// The two accumulators let the epilogue of tile j run while the MMA warp
+// accumulates tile j+1.
+//
+// Programmatic dependent launch: the producer issues the weight half of its
+// first STAGES k-tiles, then griddepcontrol.wait, then the activation half,
+// so weight streaming overlaps the previous kernel's tail.
+//
 // The epilogue works on (token, feature) pairs: in the normal orientation A
-// rows are tokens and B rows are features; with `swap` A rows are features
-// (the weight matrix streams through the M side) and B rows are tokens, which
-// is how the denoise loop runs its 50/51-token GEMMs on tensor cores.
+// rows are tokens and B rows are features; with SWAP the A rows are features
+// (the weight matrix streams through the M side) and the B rows are tokens,
+// which is how the denoise loop runs its 50/51-token GEMMs on tensor cores.
+// In the normal orientation each warp stages 32 rows x 32 columns in shared
+// memory and writes them back row-contiguous, so every store instruction
+// covers whole 32-byte sectors of a few rows; in the swapped orientation
+// consecutive lanes already hold consecutive features of one token.
+// The epilogue kind and orientation are template parameters, so each kernel
+// instantiation carries only its own epilogue code.
 #pragma once
 
 #include "common.cuh"
@@ -21,8 +36,9 @@ namespace fvb {
 
 struct GemmDev {
   int m, n, k;
-  int swap, epi, act;
+  int act;
   int k_tiles, kt_per_split, split;
+  int m_tiles, n_tiles, n_work;
   void* out;
   long long ldo;
   const float* bias;
@@ -36,248 +52,459 @@ struct GemmDev {
   int n_heads, head_dim;
   const float* rope_cs;
   const int* positions;
+  int trace;  // diagnostics: record per-CTA phase times in g_gemm_trace
 };
+
+// Diagnostics: per-CTA globaltimer stamps [start, setup done, first weight
+// TMA issued, first k-tile landed, last MMA committed, first accumulator
+// ready, last epilogue done, end] for the first GEMM_TRACE_CTAS CTAs of a
+// launch made with tracing on.
+constexpr int GEMM_TRACE_CTAS = 1024;
+__device__ unsigned long long g_gemm_trace[GEMM_TRACE_CTAS][16];
+
+__device__ __forceinline__ void trace_stamp(const GemmDev& p, int slot) {
+  if (p.trace && blockIdx.x < GEMM_TRACE_CTAS)
+    g_gemm_trace[blockIdx.x][slot] = globaltimer_ns();
+}
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
+constexpr int STAGE_PITCH = 33;  // 32-bit words per staged row
 
-__device__ __forceinline__ float apply_act(float x, int act) {
-  if (act == FVB_ACT_GELU_TANH) return gelu_tanh_f(x);
-  if (act == FVB_ACT_SILU) return silu_f(x);
+template <int ACT>
+__device__ __forceinline__ float apply_act(float x) {
+  if (ACT == FVB_ACT_GELU_TANH) return gelu_tanh_f(x);
+  if (ACT == FVB_ACT_SILU) return silu_f(x);
   return x;
 }
 
-// Epilogue for 16 accumulator values of one A row (`arow`, absolute) and B
-// rows bcol0 .. bcol0+15 (absolute).  All 32 lanes of the warp call this
-// together (shuffles in the swapped orientation).
-__device__ __forceinline__ void gemm_epilogue16(const GemmDev& p, int arow,
-                                                int bcol0, float (&v)[16],
-                                                int lane) {
-  const bool swap = p.swap != 0;
-  const int n_tok = swap ? p.n : p.m;
-  const int n_feat = swap ? p.m : p.n;
+struct Tile {
+  int m0, nt, kt0, kt1, split;
+};
 
-  if (p.epi == FVB_EPI_GEGLU || p.epi == FVB_EPI_QKV_ROPE) {
-    // Paired features: packed feature 2i and 2i+1 belong together.
-    float other[16];
-    if (swap) {
+__device__ __forceinline__ Tile decode_tile(const GemmDev& p, int w) {
+  Tile t;
+  const int mt = w % p.m_tiles;
+  const int rest = w / p.m_tiles;
+  t.nt = rest % p.n_tiles;
+  t.split = rest / p.n_tiles;
+  t.m0 = mt * GEMM_BM;
+  t.kt0 = t.split * p.kt_per_split;
+  t.kt1 = min(t.kt0 + p.kt_per_split, p.k_tiles);
+  return t;
+}
+
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+
+// Cooperative write-back of a warp's staged block of 32 rows x NW 32-bit
+// words.  Each lane moves 4 words (16 bytes), so one instruction covers
+// 128/NW rows.  All loads (staged words, destination or row_add operands) are
+// issued before any store so their latencies overlap.  Words >= NW/2 of a
+// row go hi_extra words further (the two rotary halves of a head).
+//   MODE 0: store, 1: add to an f32 destination, 2: atomic add (split-K),
+//   3: f32 store + bf16 row_add (position embedding)
+template <int NW, int MODE, typename DstFn>
+__device__ __forceinline__ void warp_writeback(
+    const uint32_t* stage, int lane, int rows_valid, int words_valid,
+    DstFn dst_of_row, int hi_extra = 0, const bf16* ra_base = nullptr,
+    int ra_mod = 1, int ra_ld = 0, int t_base = 0) {
+  constexpr int LPR = NW / 4;     // lanes per row
+  constexpr int RPI = 32 / LPR;   // rows per instruction
+  constexpr int ITER = 32 / RPI;
+  const int sub = lane % LPR, rr = lane / LPR;
+  const int w0 = sub * 4;
+  const int extra = (w0 >= NW / 2) ? hi_extra : 0;
+  const bool vec = w0 + 4 <= words_valid;
+  float val[ITER][4];
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        other[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
-    }
-    if (p.epi == FVB_EPI_GEGLU) {
-      bf16* out = reinterpret_cast<bf16*>(p.out);
-      if (!swap) {
-        const int t = arow;
-        if (t >= n_tok) return;
-        const int f0 = bcol0 >> 1;
-        if (bcol0 + 16 <= n_feat) {
-          uint32_t w[4];
+  for (int it = 0; it < ITER; ++it) {
+    const int row = it * RPI + rr;
+    const uint32_t* s = stage + row * STAGE_PITCH + w0;
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            w[i] = pack_bf16x2(gelu_tanh_f(v[4 * i]) * v[4 * i + 1],
-                               gelu_tanh_f(v[4 * i + 2]) * v[4 * i + 3]);
-          *reinterpret_cast<uint4*>(out + (long long)t * p.ldo + f0) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+    for (int w = 0; w < 4; ++w) val[it][w] = u2f(s[w]);
+    if (row < rows_valid && (MODE == 1 || MODE == 3)) {
+      if (MODE == 1) {
+        const float* d = reinterpret_cast<const float*>(dst_of_row(row) + w0 + extra);
+        if (vec) {
+          const float4 o = *reinterpret_cast<const float4*>(d);
+          val[it][0] += o.x; val[it][1] += o.y; val[it][2] += o.z; val[it][3] += o.w;
         } else {
-          for (int i = 0; i < 8; ++i)
-            if (bcol0 + 2 * i + 1 < n_feat)
-              out[(long long)t * p.ldo + f0 + i] =
-                  __float2bfloat16(gelu_tanh_f(v[2 * i]) * v[2 * i + 1]);
+#pragma unroll
+          for (int w = 0; w < 4; ++w)
+            if (w0 + w < words_valid) val[it][w] += d[w];
         }
       } else {
-        const int f = arow;
-        if ((lane & 1) || f >= n_feat) return;
+        const bf16* ra = ra_base + (long long)((t_base + row) % ra_mod) * ra_ld + w0;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = bcol0 + j;
-          if (t < n_tok)
-            out[(long long)t * p.ldo + (f >> 1)] =
-                __float2bfloat16(gelu_tanh_f(v[j]) * other[j]);
-        }
-      }
-      return;
-    }
-    // QKV + RoPE
-    const int hd = p.head_dim, half = hd >> 1;
-    const int qk_end = (p.n_heads + 1) * hd;
-    bf16* qout = reinterpret_cast<bf16*>(p.out);
-    if (!swap) {
-      const int t = arow;
-      if (t >= n_tok || bcol0 >= n_feat) return;
-      if (bcol0 < qk_end) {
-        const int hh = bcol0 / hd;
-        const int i0 = (bcol0 % hd) >> 1;  // 8 consecutive dims i0..i0+7
-        const int pos = p.positions[t];
-        const float* cs = p.rope_cs + ((long long)pos * half + i0) * 2;
-        float o1[8], o2[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float c = cs[2 * i], s = cs[2 * i + 1];
-          const float x1 = v[2 * i], x2 = v[2 * i + 1];
-          o1[i] = x1 * c - x2 * s;
-          o2[i] = x2 * c + x1 * s;
-        }
-        bf16* dst = (hh < p.n_heads)
-                        ? qout + (long long)t * p.ldo + hh * hd
-                        : p.k_out + (long long)t * p.ld_kv;
-        uint4 a = make_uint4(pack_bf16x2(o1[0], o1[1]), pack_bf16x2(o1[2], o1[3]),
-                             pack_bf16x2(o1[4], o1[5]), pack_bf16x2(o1[6], o1[7]));
-        uint4 b = make_uint4(pack_bf16x2(o2[0], o2[1]), pack_bf16x2(o2[2], o2[3]),
-                             pack_bf16x2(o2[4], o2[5]), pack_bf16x2(o2[6], o2[7]));
-        *reinterpret_cast<uint4*>(dst + i0) = a;
-        *reinterpret_cast<uint4*>(dst + i0 + half) = b;
-      } else {
-        const int d0 = bcol0 - qk_end;
-        bf16* dst = p.v_out + (long long)t * p.ld_kv + d0;
-        uint4 a = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                             pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-        uint4 b = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
-                             pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
-        *reinterpret_cast<uint4*>(dst) = a;
-        *reinterpret_cast<uint4*>(dst + 8) = b;
-      }
-    } else {
-      const int f = arow;
-      if (f >= n_feat) return;
-      if (f < qk_end) {
-        const int hh = f / hd;
-        const int within = f % hd;
-        const int i = within >> 1;
-        const bool second = within & 1;
-        bf16* dst = (hh < p.n_heads) ? qout + hh * hd : p.k_out;
-        const long long ld = (hh < p.n_heads) ? p.ldo : p.ld_kv;
-        const int dim = second ? i + half : i;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = bcol0 + j;
-          if (t >= n_tok) break;
-          const int pos = p.positions[t];
-          const float c = p.rope_cs[((long long)pos * half + i) * 2];
-          const float s = p.rope_cs[((long long)pos * half + i) * 2 + 1];
-          const float x1 = second ? other[j] : v[j];
-          const float x2 = second ? v[j] : other[j];
-          const float r = second ? (x2 * c + x1 * s) : (x1 * c - x2 * s);
-          dst[(long long)t * ld + dim] = __float2bfloat16(r);
-        }
-      } else {
-        const int d = f - qk_end;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = bcol0 + j;
-          if (t >= n_tok) break;
-          p.v_out[(long long)t * p.ld_kv + d] = __float2bfloat16(v[j]);
-        }
+        for (int w = 0; w < 4; ++w)
+          if (w0 + w < words_valid) val[it][w] += __bfloat162float(ra[w]);
       }
     }
-    return;
   }
-
-  // Unpaired epilogues: element (t, f).
-  const bool use_bias = p.bias != nullptr && (p.epi != FVB_EPI_F32_ACC ||
-                                              blockIdx.z == 0);
-  if (!swap) {
-    const int t = arow;
-    if (t >= n_tok) return;
-    const bool full = (bcol0 + 16 <= n_feat);
-    if (p.epi == FVB_EPI_BF16) {
-      bf16* out = reinterpret_cast<bf16*>(p.out) + (long long)t * p.ldo;
-      float y[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int f = bcol0 + j;
-        const float b = (use_bias && f < n_feat) ? p.bias[f] : 0.f;
-        y[j] = apply_act(p.alpha * v[j] + b, p.act);
-      }
-      if (full && (p.ldo % 8) == 0) {
-        uint4 a = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
-                             pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
-        uint4 b = make_uint4(pack_bf16x2(y[8], y[9]), pack_bf16x2(y[10], y[11]),
-                             pack_bf16x2(y[12], y[13]), pack_bf16x2(y[14], y[15]));
-        *reinterpret_cast<uint4*>(out + bcol0) = a;
-        *reinterpret_cast<uint4*>(out + bcol0 + 8) = b;
-      } else {
-        for (int j = 0; j < 16; ++j)
-          if (bcol0 + j < n_feat) out[bcol0 + j] = __float2bfloat16(y[j]);
-      }
-    } else if (p.epi == FVB_EPI_F32_STORE) {
-      float* out = reinterpret_cast<float*>(p.out) + (long long)t * p.ldo;
-      const bf16* ra = p.row_add ? p.row_add + (long long)(t % p.row_add_mod) *
-                                                   n_feat
-                                 : nullptr;
+  for (int it = 0; it < ITER; ++it) {
+    const int row = it * RPI + rr;
+    if (row >= rows_valid) continue;
+    uint32_t* d = dst_of_row(row) + w0 + extra;
+    if (MODE == 2) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int f = bcol0 + j;
-        if (f < n_feat) {
-          float y = v[j];
-          if (use_bias) y += p.bias[f];
-          if (ra) y += __bfloat162float(ra[f]);
-          out[f] = y;
-        }
-      }
-    } else {  // FVB_EPI_F32_ACC
-      float* out = reinterpret_cast<float*>(p.out) + (long long)t * p.ldo;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int f = bcol0 + j;
-        if (f < n_feat) {
-          float y = v[j];
-          if (use_bias) y += p.bias[f];
-          y *= p.alpha;
-          if (p.gate) y *= p.gate[f];
-          if (p.split > 1)
-            atomicAdd(out + f, y);
-          else
-            out[f] += y;
-        }
-      }
-    }
-  } else {
-    const int f = arow;
-    if (f >= n_feat) return;
-    const float b = use_bias ? p.bias[f] : 0.f;
-    if (p.epi == FVB_EPI_BF16) {
-      bf16* out = reinterpret_cast<bf16*>(p.out) + f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = bcol0 + j;
-        if (t < n_tok)
-          out[(long long)t * p.ldo] =
-              __float2bfloat16(apply_act(p.alpha * v[j] + b, p.act));
-      }
-    } else if (p.epi == FVB_EPI_F32_STORE) {
-      float* out = reinterpret_cast<float*>(p.out) + f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = bcol0 + j;
-        if (t < n_tok) {
-          float y = v[j] + b;
-          if (p.row_add)
-            y += __bfloat162float(
-                p.row_add[(long long)(t % p.row_add_mod) * n_feat + f]);
-          out[(long long)t * p.ldo] = y;
-        }
-      }
+      for (int w = 0; w < 4; ++w)
+        if (w0 + w < words_valid) atomicAdd(reinterpret_cast<float*>(d) + w, val[it][w]);
+    } else if (vec) {
+      *reinterpret_cast<uint4*>(d) =
+          make_uint4(__float_as_uint(val[it][0]), __float_as_uint(val[it][1]),
+                     __float_as_uint(val[it][2]), __float_as_uint(val[it][3]));
     } else {
-      float* out = reinterpret_cast<float*>(p.out) + f;
-      const float g = p.alpha * (p.gate ? p.gate[f] : 1.f);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = bcol0 + j;
-        if (t < n_tok) {
-          const float y = (v[j] + b) * g;
-          if (p.split > 1)
-            atomicAdd(out + (long long)t * p.ldo, y);
-          else
-            out[(long long)t * p.ldo] += y;
-        }
+      for (int w = 0; w < 4; ++w)
+        if (w0 + w < words_valid) d[w] = __float_as_uint(val[it][w]);
+    }
+  }
+}
+
+// Operands of one tile's epilogue that do not depend on the accumulator,
+// loaded before the accumulator is ready (while the MMA warp still runs).
+struct EpiPre {
+  float fb, fg;            // swap: this feature row's bias and gate*alpha
+  int pos;                 // normal QKV: this token row's position
+  float x0[16], y0[16];    // first chunk's gathered operands
+};
+
+template <int BN, int EPI>
+__device__ __forceinline__ void load_rope32(const GemmDev& p, int pos, int f0,
+                                            float (&cs)[32]) {
+  const int hd = p.head_dim, half = hd >> 1;
+  const int i0 = (f0 % hd) >> 1;
+  const float4* src =
+      reinterpret_cast<const float4*>(p.rope_cs + ((long long)pos * half + i0) * 2);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 q = src[j];
+    cs[4 * j] = q.x; cs[4 * j + 1] = q.y; cs[4 * j + 2] = q.z; cs[4 * j + 3] = q.w;
+  }
+}
+
+// Swapped orientation: chunk operands of 16 tokens (rotary cos/sin for query
+// and key rows, the old residual for an unsplit F32_ACC, row_add values).
+template <int EPI>
+__device__ __forceinline__ void swap_chunk_operands(const GemmDev& p, int fs,
+                                                    bool is_qk, int pair_i,
+                                                    int t0, float (&x)[16],
+                                                    float (&y)[16]) {
+  const int n_tok = p.n, n_feat = p.m;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int tt = min(t0 + j, n_tok - 1);
+    x[j] = 0.f;
+    y[j] = 0.f;
+    if (EPI == FVB_EPI_F32_STORE) {
+      if (p.row_add)
+        x[j] = __bfloat162float(p.row_add[(long long)(tt % p.row_add_mod) * n_feat + fs]);
+    } else if (EPI == FVB_EPI_F32_ACC) {
+      if (p.split == 1)
+        x[j] = reinterpret_cast<const float*>(p.out)[(long long)tt * p.ldo + fs];
+    } else if (EPI == FVB_EPI_QKV_ROPE) {
+      if (is_qk) {
+        const float2 q = *reinterpret_cast<const float2*>(
+            p.rope_cs + ((long long)p.positions[tt] * (p.head_dim >> 1) + pair_i) * 2);
+        x[j] = q.x;
+        y[j] = q.y;
       }
     }
   }
 }
 
-template <int BN, int STAGES>
+// colv: this warp's [2][BN] shared-memory column vectors (bias, gate*alpha)
+template <int BN, int EPI, bool SWAP>
+__device__ __forceinline__ void epi_prefetch(const GemmDev& p, EpiPre& e,
+                                             float* colv, int arow, int bcol0,
+                                             int split, int lane) {
+  const bool use_bias = p.bias != nullptr && (EPI != FVB_EPI_F32_ACC || split == 0);
+  if (!SWAP) {
+    const int n_feat = p.n;
+    if (EPI == FVB_EPI_BF16 || EPI == FVB_EPI_F32_STORE || EPI == FVB_EPI_F32_ACC) {
+      __syncwarp();  // the previous tile's readers are done
+#pragma unroll 1
+      for (int c = lane; c < BN; c += 32) {
+        const int fc = min(bcol0 + c, n_feat - 1);
+        colv[c] = use_bias ? __ldg(p.bias + fc) : 0.f;
+        colv[BN + c] = (EPI == FVB_EPI_F32_ACC)
+                           ? p.alpha * (p.gate ? __ldg(p.gate + fc) : 1.f) : 1.f;
+      }
+    }
+    if (EPI == FVB_EPI_QKV_ROPE) {
+      e.pos = arow < p.m ? p.positions[arow] : 0;
+      const int qk_end = (p.n_heads + 1) * p.head_dim;
+      if (bcol0 < qk_end) {
+        float cs[32];
+        load_rope32<BN, EPI>(p, e.pos, bcol0, cs);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) { e.x0[j] = cs[j]; e.y0[j] = cs[16 + j]; }
+      }
+    }
+  } else {
+    const int n_feat = p.m;
+    const int fs = min(arow, n_feat - 1);
+    e.fb = use_bias ? __ldg(p.bias + fs) : 0.f;
+    e.fg = p.alpha * (p.gate ? __ldg(p.gate + fs) : 1.f);
+    const int hd = EPI == FVB_EPI_QKV_ROPE ? p.head_dim : 2;
+    const bool is_qk = EPI == FVB_EPI_QKV_ROPE && arow < (p.n_heads + 1) * p.head_dim;
+    swap_chunk_operands<EPI>(p, fs, is_qk, (arow % hd) >> 1, bcol0, e.x0, e.y0);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Normal orientation epilogue: thread = token row (t_base + lane), BN
+// feature columns from bcol0, processed 32 at a time through the warp's
+// staging block.  Vectorised write-back needs 16-byte aligned rows; other
+// shapes use per-thread stores.
+// ---------------------------------------------------------------------------
+template <int BN, int EPI, int ACT>
+__device__ __forceinline__ void epilogue_normal(const GemmDev& p, const EpiPre& e,
+                                                const float* colv,
+                                                uint32_t taddr, uint32_t* stage,
+                                                int t_base, int bcol0, int lane) {
+  const int n_tok = p.m, n_feat = p.n;
+  const int t = t_base + lane;
+  const bool row_ok = t < n_tok;
+  const int rows_valid = min(32, n_tok - t_base);
+  uint32_t* srow = stage + lane * STAGE_PITCH;
+  const int hd = p.head_dim, half = hd >> 1;
+  const int qk_end = (p.n_heads + 1) * hd;
+  float cs[32];
+  if (EPI == FVB_EPI_QKV_ROPE) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) { cs[j] = e.x0[j]; cs[16 + j] = e.y0[j]; }
+  }
+  __syncwarp();  // column vectors visible
+#pragma unroll 1
+  for (int g = 0; g < BN / 32; ++g) {
+    const int c = g * 32;
+    const int f0 = bcol0 + c;
+    if (f0 >= n_feat) break;  // uniform across the warp
+    const int ncol = min(32, n_feat - f0);
+    uint32_t r0[16], r1[16];
+    tmem_ld16_sync(taddr + (uint32_t)c, r0);
+    tmem_ld16_sync(taddr + (uint32_t)(c + 16), r1);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[j] = u2f(r0[j]);
+      v[16 + j] = u2f(r1[j]);
+    }
+    // next group's rotary table, in flight while this group is processed
+    float cs_next[32];
+    if (EPI == FVB_EPI_QKV_ROPE && g + 1 < BN / 32 && f0 + 32 < qk_end)
+      load_rope32<BN, EPI>(p, e.pos, f0 + 32, cs_next);
+
+    if (EPI == FVB_EPI_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 2)
+        srow[j >> 1] = pack_bf16x2(apply_act<ACT>(p.alpha * v[j] + colv[c + j]),
+                                   apply_act<ACT>(p.alpha * v[j + 1] + colv[c + j + 1]));
+      __syncwarp();
+      bf16* base = reinterpret_cast<bf16*>(p.out) + (long long)t_base * p.ldo + f0;
+      if ((p.ldo % 8) == 0 && (ncol % 8) == 0) {
+        warp_writeback<16, 0>(stage, lane, rows_valid, ncol / 2, [&](int row) {
+          return reinterpret_cast<uint32_t*>(base + (long long)row * p.ldo);
+        });
+      } else if (row_ok) {
+        bf16* o = base + (long long)lane * p.ldo;
+        for (int j = 0; j < ncol; ++j) {
+          const uint32_t w = srow[j >> 1];
+          o[j] = __ushort_as_bfloat16((j & 1) ? (unsigned short)(w >> 16)
+                                              : (unsigned short)(w & 0xffff));
+        }
+      }
+    } else if (EPI == FVB_EPI_F32_STORE || EPI == FVB_EPI_F32_ACC) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float y = v[j] + colv[c + j];
+        if (EPI == FVB_EPI_F32_ACC) y *= colv[BN + c + j];
+        srow[j] = __float_as_uint(y);
+      }
+      __syncwarp();
+      float* base = reinterpret_cast<float*>(p.out) + (long long)t_base * p.ldo + f0;
+      auto dst = [&](int row) {
+        return reinterpret_cast<uint32_t*>(base + (long long)row * p.ldo);
+      };
+      if ((p.ldo % 4) == 0) {
+        if (EPI == FVB_EPI_F32_STORE) {
+          if (p.row_add)
+            warp_writeback<32, 3>(stage, lane, rows_valid, ncol, dst, 0,
+                                  p.row_add + f0, p.row_add_mod, n_feat, t_base);
+          else
+            warp_writeback<32, 0>(stage, lane, rows_valid, ncol, dst);
+        } else if (p.split > 1) {
+          warp_writeback<32, 2>(stage, lane, rows_valid, ncol, dst);
+        } else {
+          warp_writeback<32, 1>(stage, lane, rows_valid, ncol, dst);
+        }
+      } else if (row_ok) {
+        float* o = base + (long long)lane * p.ldo;
+        for (int j = 0; j < ncol; ++j) {
+          const float y = u2f(srow[j]);
+          if (EPI == FVB_EPI_F32_STORE) {
+            o[j] = p.row_add
+                       ? y + __bfloat162float(
+                                 p.row_add[(long long)(t % p.row_add_mod) * n_feat + f0 + j])
+                       : y;
+          } else if (p.split > 1) {
+            atomicAdd(o + j, y);
+          } else {
+            o[j] += y;
+          }
+        }
+      }
+    } else if (EPI == FVB_EPI_GEGLU) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 2)
+        srow[i >> 1] = pack_bf16x2(gelu_tanh_f(v[2 * i]) * v[2 * i + 1],
+                                   gelu_tanh_f(v[2 * i + 2]) * v[2 * i + 3]);
+      __syncwarp();
+      bf16* base = reinterpret_cast<bf16*>(p.out) + (long long)t_base * p.ldo + (f0 >> 1);
+      if ((p.ldo % 8) == 0 && (ncol % 16) == 0) {
+        warp_writeback<8, 0>(stage, lane, rows_valid, ncol / 4, [&](int row) {
+          return reinterpret_cast<uint32_t*>(base + (long long)row * p.ldo);
+        });
+      } else if (row_ok) {
+        bf16* o = base + (long long)lane * p.ldo;
+        for (int i = 0; 2 * i + 1 < ncol; ++i) {
+          const uint32_t w = srow[i >> 1];
+          o[i] = __ushort_as_bfloat16((i & 1) ? (unsigned short)(w >> 16)
+                                              : (unsigned short)(w & 0xffff));
+        }
+      }
+    } else {  // FVB_EPI_QKV_ROPE: n_feat, head_dim multiples of 32
+      if (f0 < qk_end) {
+        const int hh = f0 / hd;
+        const int i0 = (f0 % hd) >> 1;
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float c0 = cs[2 * i], s0 = cs[2 * i + 1];
+          const float c1 = cs[2 * i + 2], s1 = cs[2 * i + 3];
+          const float a0 = v[2 * i], b0 = v[2 * i + 1];
+          const float a1 = v[2 * i + 2], b1 = v[2 * i + 3];
+          srow[i >> 1] = pack_bf16x2(a0 * c0 - b0 * s0, a1 * c1 - b1 * s1);
+          srow[8 + (i >> 1)] = pack_bf16x2(b0 * c0 + a0 * s0, b1 * c1 + a1 * s1);
+        }
+        __syncwarp();
+        bf16* base;
+        long long ld;
+        if (hh < p.n_heads) {
+          base = reinterpret_cast<bf16*>(p.out) + (long long)t_base * p.ldo + hh * hd + i0;
+          ld = p.ldo;
+        } else {
+          base = p.k_out + (long long)t_base * p.ld_kv + i0;
+          ld = p.ld_kv;
+        }
+        // words 0..7 -> dims i0..i0+15, words 8..15 -> dims i0+half..
+        warp_writeback<16, 0>(stage, lane, rows_valid, 16,
+                              [&](int row) {
+                                return reinterpret_cast<uint32_t*>(base + (long long)row * ld);
+                              },
+                              half / 2 - 8);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) srow[j >> 1] = pack_bf16x2(v[j], v[j + 1]);
+        __syncwarp();
+        bf16* base = p.v_out + (long long)t_base * p.ld_kv + (f0 - qk_end);
+        warp_writeback<16, 0>(stage, lane, rows_valid, 16, [&](int row) {
+          return reinterpret_cast<uint32_t*>(base + (long long)row * p.ld_kv);
+        });
+      }
+      if (g + 1 < BN / 32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cs[j] = cs_next[j];
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Swapped orientation epilogue: thread = feature row f, BN token columns in
+// chunks of 16, the next chunk's gathered operands loaded one chunk ahead.
+// Consecutive lanes hold consecutive features, so per-token stores coalesce.
+// ---------------------------------------------------------------------------
+template <int BN, int EPI, int ACT>
+__device__ __forceinline__ void epilogue_swap(const GemmDev& p, const EpiPre& e,
+                                              uint32_t taddr, int f, int bcol0,
+                                              int lane) {
+  const int n_tok = p.n, n_feat = p.m;
+  const bool f_ok = f < n_feat;
+  const int fs = min(f, n_feat - 1);
+  const int hd = EPI == FVB_EPI_QKV_ROPE ? p.head_dim : 2;
+  const int qk_end = (p.n_heads + 1) * p.head_dim;
+  const bool is_qk = EPI == FVB_EPI_QKV_ROPE && f < qk_end;
+  const int pair_i = (f % hd) >> 1;
+  const bool second = (f % hd) & 1;
+  float x[16], y[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) { x[j] = e.x0[j]; y[j] = e.y0[j]; }
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 16) {
+    const int t0 = bcol0 + c;
+    if (t0 >= n_tok) break;  // uniform across the warp
+    uint32_t r[16];
+    tmem_ld16_sync(taddr + (uint32_t)c, r);
+    float xn[16], yn[16];
+    const bool more = c + 16 < BN && t0 + 16 < n_tok;
+    if (more) swap_chunk_operands<EPI>(p, fs, is_qk, pair_i, t0 + 16, xn, yn);
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = u2f(r[j]);
+    float other[16];
+    if (EPI == FVB_EPI_GEGLU || EPI == FVB_EPI_QKV_ROPE) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) other[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
+    }
+    if (f_ok) {
+      const int nj = min(16, n_tok - t0);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j < nj) {
+          const long long tt = t0 + j;
+          if (EPI == FVB_EPI_BF16) {
+            reinterpret_cast<bf16*>(p.out)[tt * p.ldo + f] =
+                __float2bfloat16(apply_act<ACT>(p.alpha * v[j] + e.fb));
+          } else if (EPI == FVB_EPI_F32_STORE) {
+            reinterpret_cast<float*>(p.out)[tt * p.ldo + f] = v[j] + e.fb + x[j];
+          } else if (EPI == FVB_EPI_F32_ACC) {
+            float* o = reinterpret_cast<float*>(p.out) + tt * p.ldo + f;
+            if (p.split > 1)
+              atomicAdd(o, (v[j] + e.fb) * e.fg);
+            else
+              *o = x[j] + (v[j] + e.fb) * e.fg;
+          } else if (EPI == FVB_EPI_GEGLU) {
+            if (!(lane & 1))
+              reinterpret_cast<bf16*>(p.out)[tt * p.ldo + (f >> 1)] =
+                  __float2bfloat16(gelu_tanh_f(v[j]) * other[j]);
+          } else if (is_qk) {
+            const int hh = f / hd;
+            const float x1 = second ? other[j] : v[j];
+            const float x2 = second ? v[j] : other[j];
+            const float rr = second ? (x2 * x[j] + x1 * y[j]) : (x1 * x[j] - x2 * y[j]);
+            const int dim = second ? pair_i + (hd >> 1) : pair_i;
+            if (hh < p.n_heads)
+              reinterpret_cast<bf16*>(p.out)[tt * p.ldo + hh * hd + dim] = __float2bfloat16(rr);
+            else
+              p.k_out[tt * p.ld_kv + dim] = __float2bfloat16(rr);
+          } else {
+            p.v_out[tt * p.ld_kv + (f - qk_end)] = __float2bfloat16(v[j]);
+          }
+        }
+      }
+    }
+    if (more) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) { x[j] = xn[j]; y[j] = yn[j]; }
+    }
+  }
+}
+
+template <int BN, int STAGES, int EPI, bool SWAP, int ACT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, const GemmDev p) {
@@ -285,105 +512,166 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   constexpr int B_BYTES = BN * GEMM_BK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t IDESC = idesc_bf16_f32(GEMM_BM, BN);
+  constexpr uint32_t TMEM_COLS = 2 * BN;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  uint64_t* tfull = empty + STAGES;   // [2]
+  uint64_t* tempty = tfull + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* stage_all = reinterpret_cast<uint32_t*>(
+      smem + STAGES * STAGE_BYTES + 256);  // [4][32][STAGE_PITCH]
+  float* colv_all = reinterpret_cast<float*>(stage_all + 4 * 32 * STAGE_PITCH);  // [4][2][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * GEMM_BM, n0 = blockIdx.y * BN;
-  const int kt0 = blockIdx.z * p.kt_per_split;
-  const int kt1 = min(kt0 + p.kt_per_split, p.k_tiles);
 
   if (threadIdx.x == 0) {
+    trace_stamp(p, 0);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tfull, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
     fence_barrier_init();
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) trace_stamp(p, 1);
 
-  if (kt1 > kt0) {
-    if (warp == 0) {
-      if (lane == 0) {
-        int it = 0;
-        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+  if (warp == 0) {
+    if (lane == 0) {
+      // the weights are the A operand in the swapped orientation
+      const CUtensorMap* mw = SWAP ? &tmA : &tmB;
+      const CUtensorMap* mx = SWAP ? &tmB : &tmA;
+      constexpr int woff = SWAP ? 0 : A_BYTES;
+      constexpr int xoff = SWAP ? A_BYTES : 0;
+      int it = 0;
+      bool alive = true;
+      bool waited = false;
+      for (int w = blockIdx.x; w < p.n_work && alive; w += gridDim.x) {
+        const Tile t = decode_tile(p, w);
+        const int n0 = t.nt * BN;
+        const int wrow = SWAP ? t.m0 : n0, xrow = SWAP ? n0 : t.m0;
+        int kt = t.kt0;
+        if (!waited) {
+          // first tile: stream the weights of the first stages before
+          // waiting for the kernel that produces the activations
+          const int npre = min(STAGES, t.kt1 - t.kt0);
+          for (int i = 0; i < npre; ++i) {
+            mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
+            tma_load_2d(smem + i * STAGE_BYTES + woff, mw,
+                        (t.kt0 + i) * GEMM_BK, wrow, &full[i]);
+          }
+          trace_stamp(p, 2);
+          griddep_wait();
+          waited = true;
+          for (int i = 0; i < npre; ++i)
+            tma_load_2d(smem + i * STAGE_BYTES + xoff, mx,
+                        (t.kt0 + i) * GEMM_BK, xrow, &full[i]);
+          it = npre;
+          kt += npre;
+        }
+        for (; kt < t.kt1; ++kt, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1)) break;
+          if (!mbar_wait(&empty[s], ph ^ 1)) { alive = false; break; }
           uint8_t* sa = smem + s * STAGE_BYTES;
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          tma_load_2d(sa, &tmA, kt * GEMM_BK, m0, &full[s]);
-          tma_load_2d(sa + A_BYTES, &tmB, kt * GEMM_BK, n0, &full[s]);
+          tma_load_2d(sa + woff, mw, kt * GEMM_BK, wrow, &full[s]);
+          tma_load_2d(sa + xoff, mx, kt * GEMM_BK, xrow, &full[s]);
         }
       }
-    } else if (warp == 1) {
-      if (lane == 0) {
-        int it = 0;
-        bool ok = true;
-        for (int kt = kt0; kt < kt1; ++kt, ++it) {
+      if (!waited) griddep_wait();
+      griddep_launch_dependents();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0, j = 0;
+      bool alive = true;
+      for (int w = blockIdx.x; w < p.n_work && alive; w += gridDim.x, ++j) {
+        const Tile t = decode_tile(p, w);
+        const int acc = j & 1;
+        if (!mbar_wait(&tempty[acc], ((j >> 1) & 1) ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(acc * BN);
+        for (int kt = t.kt0; kt < t.kt1; ++kt, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(&full[s], ph)) { alive = false; break; }
           tc_fence_after();
+          if (it == 0) trace_stamp(p, 3);
           const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
           const uint64_t da = smem_desc_sw128(sa);
           const uint64_t db = smem_desc_sw128(sa + A_BYTES);
 #pragma unroll
           for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
             // +32 bytes per K=16 step inside the 128-byte swizzled row
-            tc_mma_bf16(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2),
-                        IDESC, (kt > kt0 || kk > 0) ? 1u : 0u);
+            tc_mma_bf16(d_tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2),
+                        IDESC, (kt > t.kt0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty[s]);
         }
-        if (ok) tc_commit(tfull);
+        if (alive) tc_commit(&tfull[acc]);
       }
-    } else {
-      const int q = warp & 3;
-      const bool ok = mbar_wait(tfull, 0);
-      __syncwarp();
-      if (ok) {
-        tc_fence_after();
-        const int arow = m0 + q * 32 + lane;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          float v[16];
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-          gemm_epilogue16(p, arow, n0 + c, v, lane);
-        }
-      }
+      trace_stamp(p, 4);
     }
+  } else {
+    const int q = warp & 3;
+    uint32_t* stage = stage_all + q * 32 * STAGE_PITCH;
+    float* colv = colv_all + q * 2 * BN;
+    griddep_wait();
+    int j = 0;
+    for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, ++j) {
+      const Tile t = decode_tile(p, w);
+      const int acc = j & 1;
+      EpiPre pre;
+      epi_prefetch<BN, EPI, SWAP>(p, pre, colv, t.m0 + q * 32 + lane,
+                                  t.nt * BN, t.split, lane);
+      const bool ok = mbar_wait(&tfull[acc], (j >> 1) & 1);
+      __syncwarp();
+      if (!ok) break;
+      tc_fence_after();
+      if (j == 0 && warp == 2 && lane == 0) trace_stamp(p, 5);
+      const uint32_t taddr =
+          tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if (SWAP)
+        epilogue_swap<BN, EPI, ACT>(p, pre, taddr, t.m0 + q * 32 + lane,
+                                    t.nt * BN, lane);
+      else
+        epilogue_normal<BN, EPI, ACT>(p, pre, colv, taddr, stage, t.m0 + q * 32,
+                                      t.nt * BN, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (warp == 2 && lane == 0) trace_stamp(p, 6);
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_stamp(p, 7);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
 template <int BN>
 struct GemmCfg {
   static constexpr int STAGES = (BN == 64) ? 8 : (BN == 128 ? 6 : 4);
-  static constexpr int SMEM =
-      STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 1024 + 256;
+  static constexpr int SMEM = STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) +
+                              1024 + 256 + 4 * 32 * STAGE_PITCH * 4 + 4 * 2 * BN * 4;
 };
 
 }  // namespace fvb

@@ -198,6 +198,13 @@ int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
                      const float* bias, int32_t act, int32_t mode,
                      float alpha, void* out, int64_t ldo, void* stream);
 
+/* Diagnostics: the next fvb_gemm launch records per-CTA phase timestamps
+ * (globaltimer ns: start, setup, first TMA issued, first k-tile landed, last
+ * MMA committed, accumulator ready, epilogue done, end) for its first 1024
+ * CTAs; fvb_gemm_trace_read copies them (8 x uint64 per CTA) to the host. */
+int fvb_gemm_trace_next(void);
+int fvb_gemm_trace_read(uint64_t* host_out, int32_t max_ctas);
+
 /* Status and diagnostics. */
 int fvb_get_device_status(int* status, int reset);
 const char* fvb_last_error(void);
