@@ -29,7 +29,8 @@ class GemmArgs(C.Structure):
                 ('row_add_mod', C.c_int32), ('k_out', C.c_void_p),
                 ('v_out', C.c_void_p), ('ld_kv', C.c_int64),
                 ('n_heads', C.c_int32), ('head_dim', C.c_int32),
-                ('rope_cs', C.c_void_p), ('positions', C.c_void_p)]
+                ('rope_cs', C.c_void_p), ('positions', C.c_void_p),
+                ('workspace', C.c_void_p), ('workspace_bytes', C.c_int64)]
 
 
 class AttnArgs(C.Structure):
@@ -51,6 +52,7 @@ class AttnArgs(C.Structure):
 
 EXPORTS = {
     'fvb_gemm': (C.c_int, [C.POINTER(GemmArgs), C.c_void_p]),
+    'fvb_gemm_workspace_bytes': (C.c_int64, [C.POINTER(GemmArgs)]),
     'fvb_attention': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),
     'fvb_attention_workspace_bytes': (C.c_int64, [C.POINTER(AttnArgs)]),
     'fvb_attention_combine': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),

@@ -326,32 +326,57 @@ __global__ void __launch_bounds__(ATT_THREADS)
   }
 }
 
-// One CTA per (batch*head, query row); HD threads max 256.
+// One CTA per (batch*head, query row), HD (or 96) threads: the split
+// weights are computed once into shared memory, then every thread sums its
+// dimension over the splits with independent loads.
+constexpr int ATT_MAX_SPLITS = 64;
 template <int HD>
 __global__ void attn_combine_kernel(const AttnDev p) {
+  __shared__ float w_s[ATT_MAX_SPLITS];
+  __shared__ float inv_l;
   griddep_wait();
   griddep_launch_dependents();
   const int row = blockIdx.x;  // over batch*heads*n_q
   const int d = threadIdx.x;
   const long long rows = (long long)p.batch * p.heads * p.n_q;
-  float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s)
-    M = fmaxf(M, p.part_ml[((long long)s * rows + row) * 2]);
-  float L = 0.f, acc = 0.f;
-  for (int s = 0; s < p.splits; ++s) {
-    const float m = p.part_ml[((long long)s * rows + row) * 2];
-    const float l = p.part_ml[((long long)s * rows + row) * 2 + 1];
-    if (l > 0.f) {
-      const float w = exp2f(m - M);
-      L += l * w;
-      if (d < HD) acc += w * p.part_o[((long long)s * rows + row) * HD + d];
+  if (threadIdx.x < 32) {
+    float m[2], l[2];
+    float M = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int s = threadIdx.x + 32 * i;
+      m[i] = -INFINITY;
+      l[i] = 0.f;
+      if (s < p.splits) {
+        const float2 ml = *reinterpret_cast<const float2*>(
+            p.part_ml + ((long long)s * rows + row) * 2);
+        m[i] = ml.x;
+        l[i] = ml.y;
+      }
+      if (l[i] > 0.f) M = fmaxf(M, m[i]);
     }
+    M = warp_max(M);
+    float L = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int s = threadIdx.x + 32 * i;
+      const float w = (l[i] > 0.f) ? exp2f(m[i] - M) : 0.f;
+      if (s < ATT_MAX_SPLITS) w_s[s] = w;
+      L += l[i] * w;
+    }
+    L = warp_sum(L);
+    if (threadIdx.x == 0) inv_l = L > 0.f ? 1.f / L : 0.f;
   }
+  __syncthreads();
   const int bh = row / p.n_q, r = row % p.n_q;
   const int b = bh / p.heads, h = bh % p.heads;
   if (d < HD) {
+    float acc = 0.f;
+    const float* po = p.part_o + (long long)row * HD + d;
+#pragma unroll 8
+    for (int s = 0; s < p.splits; ++s) acc += w_s[s] * po[(long long)s * rows * HD];
     bf16* go = p.o + ((long long)b * p.q_br + r) * p.o_rs + h * p.o_hs + d;
-    *go = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+    *go = __float2bfloat16(acc * inv_l);
   }
 }
 

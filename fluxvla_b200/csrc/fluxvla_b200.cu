@@ -179,6 +179,14 @@ int fvb_gemm_trace_read(uint64_t* host_out, int32_t max_ctas) {
   return FVB_OK;
 }
 
+int64_t fvb_gemm_workspace_bytes(const fvb_gemm_args* a) {
+  if (!a || a->m <= 0 || a->n <= 0) return -1;
+  if (!a->swap || a->epilogue == FVB_EPI_F32_ACC) return 0;
+  const long long tiles = ((a->m + fvb::GEMM_BM - 1) / fvb::GEMM_BM) *
+                          ((a->n + 63) / 64);
+  return tiles * (64 * fvb::GEMM_BM * 4 + 4);
+}
+
 int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   if (!a) return fail(FVB_ERR_INVALID_ARG, "args is NULL");
   if (!a->a || !a->b || !a->out)
@@ -193,9 +201,6 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: operands must be 16B aligned");
   if (a->epilogue < FVB_EPI_BF16 || a->epilogue > FVB_EPI_QKV_ROPE)
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: bad epilogue %d", a->epilogue);
-  const int split = a->split_k > 1 ? a->split_k : 1;
-  if (split > 1 && a->epilogue != FVB_EPI_F32_ACC)
-    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: split_k needs FVB_EPI_F32_ACC");
   const int n_feat = a->swap ? a->m : a->n;
   if (a->epilogue == FVB_EPI_GEGLU && (n_feat & 1))
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: GEGLU needs an even feature count");
@@ -229,6 +234,30 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   if (bn != 64 && bn != 128 && bn != 256)
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: block_n must be 64/128/256");
 
+  // K splits: F32_ACC adds atomically into its output; a swapped GEMM with
+  // any other epilogue reduces its splits in the workspace
+  const int k_tiles = (a->k + fvb::GEMM_BK - 1) / fvb::GEMM_BK;
+  const int tiles_mn = ((a->m + fvb::GEMM_BM - 1) / fvb::GEMM_BM) * ((a->n + bn - 1) / bn);
+  const bool ws_split = a->swap && a->epilogue != FVB_EPI_F32_ACC;
+  int split = a->split_k;
+  if (split <= 0) {
+    split = 1;
+    if (a->swap && (!ws_split || a->workspace))
+      split = sm_count() / tiles_mn > 1 ? sm_count() / tiles_mn : 1;
+  }
+  if (split > k_tiles) split = k_tiles;
+  int kt_per_split = (k_tiles + split - 1) / split;
+  split = (k_tiles + kt_per_split - 1) / kt_per_split;
+  if (split > 1 && a->epilogue != FVB_EPI_F32_ACC) {
+    if (!a->swap)
+      return fail(FVB_ERR_INVALID_ARG,
+                  "fvb_gemm: split_k > 1 needs FVB_EPI_F32_ACC or swap");
+    const long long need = (long long)tiles_mn * (bn * fvb::GEMM_BM * 4 + 4);
+    if (!a->workspace || a->workspace_bytes < need || !aligned16(a->workspace))
+      return fail(FVB_ERR_WORKSPACE,
+                  "fvb_gemm: split-K needs a zero-filled %lld-byte workspace", need);
+  }
+
   CUtensorMap ma, mb;
   int r = make_map(&ma, a->a, a->m, a->k, a->lda, fvb::GEMM_BM);
   if (r) return r;
@@ -238,9 +267,13 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   fvb::GemmDev d;
   d.m = a->m; d.n = a->n; d.k = a->k;
   d.act = a->act;
-  d.k_tiles = (a->k + fvb::GEMM_BK - 1) / fvb::GEMM_BK;
-  d.kt_per_split = (d.k_tiles + split - 1) / split;
-  d.split = (d.k_tiles + d.kt_per_split - 1) / d.kt_per_split;
+  d.k_tiles = k_tiles;
+  d.kt_per_split = kt_per_split;
+  d.split = split;
+  d.ws = reinterpret_cast<float*>(a->workspace);
+  d.ws_cnt = d.ws ? reinterpret_cast<unsigned*>(
+                        d.ws + (long long)tiles_mn * bn * fvb::GEMM_BM)
+                  : nullptr;
   d.out = a->out; d.ldo = a->ldo;
   d.bias = a->bias; d.gate = a->gate; d.alpha = a->alpha;
   d.row_add = reinterpret_cast<const bf16*>(a->row_add);
@@ -307,6 +340,7 @@ static int attn_prepare(const fvb_attn_args* a, fvb::AttnDev* d) {
   const int nkb = (a->n_kv + fvb::ATT_BN - 1) / fvb::ATT_BN;
   int splits = a->kv_splits > 1 ? a->kv_splits : 1;
   if (splits > nkb) splits = nkb;
+  if (splits > fvb::ATT_MAX_SPLITS) splits = fvb::ATT_MAX_SPLITS;
   d->blocks_per_split = (nkb + splits - 1) / splits;
   d->splits = (nkb + d->blocks_per_split - 1) / d->blocks_per_split;
   const long long rows = (long long)a->batch * a->heads * a->n_q;

@@ -52,8 +52,17 @@ struct GemmDev {
   int n_heads, head_dim;
   const float* rope_cs;
   const int* positions;
+  // split-K fixup of swapped non-additive epilogues: f32 partial tiles
+  // [m_tiles*n_tiles][BN tokens][128 features] and one arrival counter per
+  // tile; all zero between launches (the last CTA of a tile re-zeroes both)
+  float* ws;
+  unsigned* ws_cnt;
   int trace;  // diagnostics: record per-CTA phase times in g_gemm_trace
 };
+
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
 
 // Diagnostics: per-CTA globaltimer stamps [start, setup done, first weight
 // TMA issued, first k-tile landed, last MMA committed, first accumulator
@@ -428,10 +437,10 @@ __device__ __forceinline__ void epilogue_normal(const GemmDev& p, const EpiPre& 
 // chunks of 16, the next chunk's gathered operands loaded one chunk ahead.
 // Consecutive lanes hold consecutive features, so per-token stores coalesce.
 // ---------------------------------------------------------------------------
-template <int BN, int EPI, int ACT>
+template <int BN, int EPI, int ACT, bool FROM_WS>
 __device__ __forceinline__ void epilogue_swap(const GemmDev& p, const EpiPre& e,
-                                              uint32_t taddr, int f, int bcol0,
-                                              int lane) {
+                                              uint32_t taddr, const float* wst,
+                                              int f, int bcol0, int lane) {
   const int n_tok = p.n, n_feat = p.m;
   const bool f_ok = f < n_feat;
   const int fs = min(f, n_feat - 1);
@@ -448,7 +457,14 @@ __device__ __forceinline__ void epilogue_swap(const GemmDev& p, const EpiPre& e,
     const int t0 = bcol0 + c;
     if (t0 >= n_tok) break;  // uniform across the warp
     uint32_t r[16];
-    tmem_ld16_sync(taddr + (uint32_t)c, r);
+    if (FROM_WS) {
+      const int fr = f & (GEMM_BM - 1);
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        r[j] = __float_as_uint(__ldcg(wst + (c + j) * GEMM_BM + fr));
+    } else {
+      tmem_ld16_sync(taddr + (uint32_t)c, r);
+    }
     float xn[16], yn[16];
     const bool more = c + 16 < BN && t0 + 16 < n_tok;
     if (more) swap_chunk_operands<EPI>(p, fs, is_qk, pair_i, t0 + 16, xn, yn);
@@ -525,6 +541,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint32_t* stage_all = reinterpret_cast<uint32_t*>(
       smem + STAGES * STAGE_BYTES + 256);  // [4][32][STAGE_PITCH]
   float* colv_all = reinterpret_cast<float*>(stage_all + 4 * 32 * STAGE_PITCH);  // [4][2][BN]
+  volatile int* fix_flag = reinterpret_cast<volatile int*>(colv_all + 4 * 2 * BN);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -645,9 +662,42 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (j == 0 && warp == 2 && lane == 0) trace_stamp(p, 5);
       const uint32_t taddr =
           tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if (SWAP && EPI != FVB_EPI_F32_ACC && p.split > 1) {
+        // split-K: add this split's partial into the tile workspace ...
+        const int tile_mn = w % (p.m_tiles * p.n_tiles);
+        float* wst = p.ws + (long long)tile_mn * BN * GEMM_BM;
+        const int fr = q * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16_sync(taddr + (uint32_t)c, r);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj)
+            atomicAdd(wst + (c + jj) * GEMM_BM + fr, u2f(r[jj]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        // ... and the last split to arrive runs the epilogue on the sum
+        __threadfence();
+        epi_bar_sync();
+        if (warp == 2 && lane == 0)
+          *fix_flag = (atomicAdd(p.ws_cnt + tile_mn, 1u) == (unsigned)(p.split - 1));
+        epi_bar_sync();
+        if (*fix_flag) {
+          __threadfence();
+          epilogue_swap<BN, EPI, ACT, true>(p, pre, 0, wst, t.m0 + fr,
+                                            t.nt * BN, lane);
+#pragma unroll 4
+          for (int c = 0; c < BN; ++c) wst[c * GEMM_BM + fr] = 0.f;
+          if (warp == 2 && lane == 0) p.ws_cnt[tile_mn] = 0u;
+        }
+        continue;
+      }
       if (SWAP)
-        epilogue_swap<BN, EPI, ACT>(p, pre, taddr, t.m0 + q * 32 + lane,
-                                    t.nt * BN, lane);
+        epilogue_swap<BN, EPI, ACT, false>(p, pre, taddr, nullptr,
+                                           t.m0 + q * 32 + lane, t.nt * BN,
+                                           lane);
       else
         epilogue_normal<BN, EPI, ACT>(p, pre, colv, taddr, stage, t.m0 + q * 32,
                                       t.nt * BN, lane);
@@ -671,7 +721,7 @@ template <int BN>
 struct GemmCfg {
   static constexpr int STAGES = (BN == 64) ? 8 : (BN == 128 ? 6 : 4);
   static constexpr int SMEM = STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) +
-                              1024 + 256 + 4 * 32 * STAGE_PITCH * 4 + 4 * 2 * BN * 4;
+                              1024 + 256 + 4 * 32 * STAGE_PITCH * 4 + 4 * 2 * BN * 4 + 16;
 };
 
 }  // namespace fvb

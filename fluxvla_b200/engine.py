@@ -198,6 +198,12 @@ class PI0EngineB200:
         B['a_emb'] = z(self.A, We)
         B['at_h'] = z(self.A, We)
         B['e_fin'] = z(S, We, dt=F32)
+        # split-K workspace of the swapped loop GEMMs (zeroed once, left
+        # zeroed by every GEMM): sized for the widest one (gate/up)
+        ws = max(ops.gemm_workspace_bytes(2 * cfg.exp_mlp, S, True, EPI_GEGLU),
+                 ops.gemm_workspace_bytes(cfg.heads * hd + 2 * hd, S, True,
+                                          EPI_QKV_ROPE))
+        B['gemm_ws'] = z(ws, dt=torch.uint8)
         max_pos = E + S + 8
         B['rope'] = rope_table(max_pos, hd, device=d)
         self.B = B
@@ -329,11 +335,12 @@ class PI0EngineB200:
             ops.small_linear(B['x_t'], P['action_in_w'], B['a_emb'],
                              bias=P['action_in_b'], mode=1)
             ops.gemm(P['action_time_in_w'][:, :We], B['a_emb'], B['at_h'],
-                     swap=True, bias=self.step_bias[k], act=ACT_SILU)
+                     swap=True, bias=self.step_bias[k], act=ACT_SILU,
+                     split_k=0, workspace=B['gemm_ws'])
             res.zero_()
             ops.gemm(P['action_time_out_w'], B['at_h'], res[off:],
                      epilogue=EPI_F32_ACC, swap=True,
-                     bias=P['action_time_out_b'], split_k=4)
+                     bias=P['action_time_out_b'], split_k=0)
             if off:
                 res[:off].copy_(B['state_emb'])
         def attn(kc, vc):
@@ -361,7 +368,7 @@ class PI0EngineB200:
                      positions=B['pos_suffix'])
             ops.attention(attn(kc, vc))
             ops.gemm(P[p + 'o_w'], B['e_ao'], res, swap=True,
-                     epilogue=EPI_F32_ACC, split_k=16,
+                     epilogue=EPI_F32_ACC, split_k=0,
                      gate=m_in[2 * We:] if ada else None)
             if ada:
                 ops.norm(NORM_ADA_RMS, res, B['e_xn'], mod=m_post)
@@ -370,7 +377,7 @@ class PI0EngineB200:
             ops.gemm(P[p + 'gu'], B['e_xn'], B['e_h'], swap=True,
                      epilogue=EPI_GEGLU)
             ops.gemm(P[p + 'down_w'], B['e_h'], res, swap=True,
-                     epilogue=EPI_F32_ACC, split_k=16,
+                     epilogue=EPI_F32_ACC, split_k=0,
                      gate=m_post[2 * We:] if ada else None)
         fin = B['e_fin'][off:]
         if ada:

@@ -45,8 +45,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
          k_out: Optional[torch.Tensor] = None,
          v_out: Optional[torch.Tensor] = None, n_heads: int = 0,
          head_dim: int = 0, rope_cs: Optional[torch.Tensor] = None,
-         positions: Optional[torch.Tensor] = None) -> None:
-    """C[M,N] = A[M,K] @ B[N,K]^T with a fused epilogue (see fvb_gemm)."""
+         positions: Optional[torch.Tensor] = None,
+         workspace: Optional[torch.Tensor] = None) -> None:
+    """C[M,N] = A[M,K] @ B[N,K]^T with a fused epilogue (see fvb_gemm).
+    split_k=0 picks the split automatically for swapped GEMMs; a swapped
+    split GEMM with a non-additive epilogue needs ``workspace`` (a zeroed
+    uint8 tensor of gemm_workspace_bytes(...), left zeroed by the call)."""
     lda = _rowmajor(a, 'a', BF16)
     ldb = _rowmajor(b, 'b', BF16)
     if a.shape[1] != b.shape[1]:
@@ -65,8 +69,15 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
                     v_out=_ptr(v_out),
                     ld_kv=0 if k_out is None else k_out.stride(0),
                     n_heads=n_heads, head_dim=head_dim, rope_cs=_ptr(rope_cs),
-                    positions=_ptr(positions))
+                    positions=_ptr(positions), workspace=_ptr(workspace),
+                    workspace_bytes=0 if workspace is None else
+                    workspace.numel() * workspace.element_size())
     check(_lib.lib().fvb_gemm(C.byref(args), _stream()))
+
+
+def gemm_workspace_bytes(m: int, n: int, swap: bool, epilogue: int) -> int:
+    args = GemmArgs(m=m, n=n, swap=int(swap), epilogue=epilogue)
+    return int(_lib.lib().fvb_gemm_workspace_bytes(C.byref(args)))
 
 
 def attn_args(q, k, v, o, *, n_q, n_kv, heads, group, head_dim, scale,

@@ -61,7 +61,8 @@ typedef struct fvb_gemm_args {
   int32_t swap;
   int32_t epilogue; /* FVB_EPI_* */
   int32_t act;      /* FVB_ACT_*, FVB_EPI_BF16 only */
-  int32_t split_k;  /* >1 only with FVB_EPI_F32_ACC (atomic accumulation) */
+  int32_t split_k;  /* K splits: F32_ACC accumulates atomically into out;
+                     * swapped non-additive epilogues need the workspace   */
   int32_t block_n;  /* 0 = auto, else 64 / 128 / 256 */
   void* out;        /* see epilogues */
   int64_t ldo;      /* elements */
@@ -81,6 +82,15 @@ typedef struct fvb_gemm_args {
   int32_t head_dim;
   const float* rope_cs;      /* [max_pos, head_dim/2, 2] (cos, sin) f32 */
   const int32_t* positions;  /* [tokens] */
+  /* Split-K of a swapped GEMM with a non-additive epilogue (BF16, GEGLU,
+   * QKV_ROPE, F32_STORE) sums the splits in this workspace and lets the last
+   * split of each tile apply the epilogue.  Size from
+   * fvb_gemm_workspace_bytes(); it must be zero-filled before its first use
+   * and is left zero-filled by every call.  Calls sharing one workspace must
+   * not overlap on the GPU.  split_k = 0 picks the split count automatically
+   * (enough tiles to fill the GPU) for swapped GEMMs.                       */
+  void* workspace;
+  int64_t workspace_bytes;
 } fvb_gemm_args;
 
 /* tcgen05/TMEM tensor-core GEMM with fused epilogues.
@@ -93,6 +103,8 @@ typedef struct fvb_gemm_args {
  * matmul_triton_ops.py:763), matmul_bias_silu :231, matmul_qkv_rope :309,
  * matmul_res_gate :345, matmul_gate :375.                                  */
 int fvb_gemm(const fvb_gemm_args* args, void* stream);
+/* Workspace bytes fvb_gemm needs for these arguments (0 when none). */
+int64_t fvb_gemm_workspace_bytes(const fvb_gemm_args* args);
 
 typedef struct fvb_attn_args {
   /* Element (row r, head h, dim d) of Q is

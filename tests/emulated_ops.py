@@ -24,7 +24,7 @@ def _act(x, act):
 def gemm(a, b, out, *, epilogue=EPI_BF16, swap=False, act=0, bias=None,
          gate=None, alpha=1.0, split_k=1, block_n=0, row_add=None,
          row_add_mod=0, k_out=None, v_out=None, n_heads=0, head_dim=0,
-         rope_cs=None, positions=None):
+         rope_cs=None, positions=None, workspace=None):
     _count[0] += 1
     acc = a.float() @ b.float().t()
     if swap:
@@ -118,6 +118,10 @@ def attention_workspace_bytes(args):
     return 16
 
 
+def gemm_workspace_bytes(m, n, swap, epilogue):
+    return 16
+
+
 def norm(mode, x, out, *, w=None, b=None, mod=None, eps=1e-6):
     _count[0] += 1
     D = x.shape[1]
@@ -167,6 +171,7 @@ def launch_count():
 def install(monkeypatch):
     from fluxvla_b200 import engine, ops
     for name in ['gemm', 'attn_args', 'attention', 'attention_workspace_bytes',
+                 'gemm_workspace_bytes',
                  'norm', 'patchify', 'embed_tokens', 'small_linear',
                  'launch_count']:
         monkeypatch.setattr(ops, name, globals()[name])

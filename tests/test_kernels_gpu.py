@@ -298,3 +298,58 @@ def test_patchify_embed_small_linear():
     ops.small_linear(x, w, acc, bias=bias, mode=2, alpha=-0.1)
     torch.cuda.synchronize()
     torch.testing.assert_close(acc, ref, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize('split', [0, 3, 16])
+def test_gemm_swap_split_fixup(split):
+    """Swapped split-K GEMMs with non-additive epilogues reduce their splits
+    in the workspace; results match and the workspace is left zeroed."""
+    torch.manual_seed(12)
+    T, K, H, hd = 51, 1024, 8, 256
+    x = rnd(T, K)
+    ws = torch.zeros(ops.gemm_workspace_bytes(4096 * 2, T, True, EPI_GEGLU),
+                     dtype=torch.uint8, device=DEV)
+    # GeGLU
+    g, u = rnd(4096, K, std=0.02), rnd(4096, K, std=0.02)
+    out = torch.empty(T, 4096, device=DEV, dtype=torch.bfloat16)
+    for _ in range(2):
+        ops.gemm(pack_geglu(g, u), x, out, epilogue=EPI_GEGLU, swap=True,
+                 split_k=split, workspace=ws)
+    xf = x.float()
+    ref = torch.nn.functional.gelu(xf @ g.float().t(), approximate='tanh') * (
+        xf @ u.float().t())
+    torch.cuda.synchronize()
+    close(out, ref)
+    assert ws.count_nonzero() == 0
+    # SiLU with bias
+    w = rnd(1024, K, std=0.02)
+    bias = torch.randn(1024, device=DEV) * 0.1
+    out = torch.empty(T, 1024, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(w, x, out, swap=True, bias=bias, act=ACT_SILU, split_k=split,
+             workspace=ws)
+    torch.cuda.synchronize()
+    close(out, torch.nn.functional.silu(xf @ w.float().t() + bias))
+    assert ws.count_nonzero() == 0
+    # QKV + RoPE
+    qw, kw, vw = rnd(H * hd, K, std=0.02), rnd(hd, K, std=0.02), rnd(
+        hd, K, std=0.02)
+    pos = (torch.arange(T, device=DEV) + 816).int()
+    cs = rope_table(1024, hd, device=DEV)
+    q = torch.empty(T, H * hd, device=DEV, dtype=torch.bfloat16)
+    kc = torch.zeros(T, hd, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros(T, hd, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(pack_qkv(qw, kw, vw, hd), x, q, swap=True, epilogue=EPI_QKV_ROPE,
+             k_out=kc, v_out=vc, n_heads=H, head_dim=hd, rope_cs=cs,
+             positions=pos, split_k=split, workspace=ws)
+    torch.cuda.synchronize()
+    close(q.view(T, H, hd), _rope_ref((xf @ qw.float().t()).view(T, H, hd), pos, hd))
+    close(kc, _rope_ref((xf @ kw.float().t()).view(T, 1, hd), pos, hd)[:, 0])
+    close(vc, xf @ vw.float().t())
+    assert ws.count_nonzero() == 0
+
+
+def test_gemm_split_without_workspace_is_rejected():
+    x, w = rnd(51, 1024), rnd(1024, 1024, std=0.02)
+    out = torch.empty(51, 1024, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match='workspace'):
+        ops.gemm(w, x, out, swap=True, split_k=4)
