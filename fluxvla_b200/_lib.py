@@ -50,7 +50,26 @@ class AttnArgs(C.Structure):
                 ('workspace', C.c_void_p), ('workspace_bytes', C.c_int64)]
 
 
+class ExpertArgs(C.Structure):
+    _fields_ = [('n_layers', C.c_int32), ('n_tok', C.c_int32),
+                ('width', C.c_int32), ('mlp', C.c_int32),
+                ('heads', C.c_int32), ('head_dim', C.c_int32),
+                ('n_prefix', C.c_int32), ('w_qkv', C.c_void_p),
+                ('w_o', C.c_void_p), ('w_gu', C.c_void_p),
+                ('w_down', C.c_void_p), ('in_scale', C.c_void_p),
+                ('post_scale', C.c_void_p), ('qkv_bias', C.c_void_p),
+                ('gu_bias', C.c_void_p), ('o_gate', C.c_void_p),
+                ('down_gate', C.c_void_p), ('eps', C.c_float),
+                ('x', C.c_void_p), ('k_cache', C.c_void_p),
+                ('v_cache', C.c_void_p), ('cache_rows', C.c_int64),
+                ('key_valid', C.c_void_p), ('blocks', C.c_void_p),
+                ('positions', C.c_void_p), ('rope_cs', C.c_void_p),
+                ('workspace', C.c_void_p), ('workspace_bytes', C.c_int64)]
+
+
 EXPORTS = {
+    'fvb_expert_step': (C.c_int, [C.POINTER(ExpertArgs), C.c_void_p]),
+    'fvb_expert_workspace_bytes': (C.c_int64, [C.POINTER(ExpertArgs)]),
     'fvb_gemm': (C.c_int, [C.POINTER(GemmArgs), C.c_void_p]),
     'fvb_gemm_workspace_bytes': (C.c_int64, [C.POINTER(GemmArgs)]),
     'fvb_attention': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),

@@ -10,6 +10,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "elementwise.cuh"
+#include "expert_mega.cuh"
 #include "gemm_tc.cuh"
 
 namespace {
@@ -473,6 +474,130 @@ int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Persistent expert step
+// ---------------------------------------------------------------------------
+namespace {
+
+struct ExpertLayout {
+  fvb::mega::Params p;
+  long long bytes;
+};
+
+int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
+  using namespace fvb::mega;
+  if (!a) return fail(FVB_ERR_INVALID_ARG, "args is NULL");
+  if (a->n_layers <= 0 || a->n_layers > 64 || a->n_tok <= 0 || a->n_tok > TOK ||
+      a->width % 128 || a->width <= 0 || a->mlp % 64 || a->mlp <= 0 ||
+      a->head_dim != 256 || a->heads <= 0 || a->n_prefix < 0)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_expert_step: unsupported shape");
+  Params& p = out->p;
+  p.n_layers = a->n_layers; p.n_tok = a->n_tok; p.width = a->width;
+  p.mlp = a->mlp; p.heads = a->heads; p.hd = a->head_dim;
+  p.n_prefix = a->n_prefix;
+  const int G = sm_count();
+  const int rows[N_GEMM] = {(a->heads + 2) * a->head_dim, a->width, 2 * a->mlp,
+                            a->width};
+  const int ks[N_GEMM] = {a->width, a->heads * a->head_dim, a->width, a->mlp};
+  for (int i = 0; i < N_GEMM; ++i) {
+    Gemm& g = p.g[i];
+    g.rows = rows[i];
+    g.m_tiles = rows[i] / 128;
+    g.k_tiles = ks[i] / 64;
+    int sp = G / g.m_tiles > 1 ? G / g.m_tiles : 1;
+    if (sp > g.k_tiles) sp = g.k_tiles;
+    g.kt_per = (g.k_tiles + sp - 1) / sp;
+    if (g.kt_per > MAX_KT) g.kt_per = MAX_KT;
+    g.splits = (g.k_tiles + g.kt_per - 1) / g.kt_per;
+    g.items = g.m_tiles * g.splits;
+  }
+  p.in_scale = a->in_scale; p.post_scale = a->post_scale;
+  p.qkv_bias = a->qkv_bias; p.gu_bias = a->gu_bias;
+  p.o_gate = a->o_gate; p.down_gate = a->down_gate;
+  p.eps = a->eps; p.x = a->x;
+  p.kc = (const bf16*)a->k_cache; p.vc = (const bf16*)a->v_cache;
+  p.cache_layer = a->cache_rows * a->head_dim;
+  p.key_valid = a->key_valid; p.blocks = a->blocks; p.positions = a->positions;
+  p.rope_cs = a->rope_cs;
+  p.scale_log2 = (1.f / sqrtf((float)a->head_dim)) * 1.4426950408889634f;
+  p.nkb = (a->n_prefix + a->n_tok + 63) / 64;
+  // workspace carve-up (256-byte aligned pieces)
+  char* base = (char*)a->workspace;
+  long long off = 0;
+  auto take = [&](long long n) {
+    long long o = off;
+    off += (n + 255) & ~255ll;
+    return base ? base + o : nullptr;
+  };
+  p.acc_qkv = (float*)take((long long)TOK * rows[0] * 4);
+  p.acc_gu = (float*)take((long long)TOK * rows[2] * 4);
+  p.ss_in = (float*)take(TOK * 4);
+  p.ss_post = (float*)take(TOK * 4);
+  p.part_o = (float*)take((long long)a->heads * p.nkb * TOK * a->head_dim * 4);
+  p.part_ml = (float*)take((long long)a->heads * p.nkb * TOK * 2 * 4);
+  p.attn = (bf16*)take((long long)TOK * a->heads * a->head_dim * 2);
+  p.bar = (unsigned*)take(64);
+  out->bytes = off;
+  return FVB_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t fvb_expert_workspace_bytes(const fvb_expert_args* a) {
+  ExpertLayout L;
+  fvb_expert_args tmp = *a;
+  tmp.workspace = nullptr;
+  if (expert_prepare(&tmp, &L)) return -1;
+  return L.bytes;
+}
+
+extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
+  using namespace fvb::mega;
+  ExpertLayout L;
+  int r = expert_prepare(a, &L);
+  if (r) return r;
+  if (!a->w_qkv || !a->w_o || !a->w_gu || !a->w_down || !a->in_scale ||
+      !a->post_scale || !a->x || !a->k_cache || !a->v_cache || !a->blocks ||
+      !a->positions || !a->rope_cs)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_expert_step: NULL operand");
+  if (!a->workspace || a->workspace_bytes < L.bytes || !aligned16(a->workspace))
+    return fail(FVB_ERR_WORKSPACE, "fvb_expert_step: workspace needs %lld bytes",
+                L.bytes);
+  const Params& p = L.p;
+  CUtensorMap maps[N_GEMM];
+  const void* w[N_GEMM] = {a->w_qkv, a->w_o, a->w_gu, a->w_down};
+  for (int i = 0; i < N_GEMM; ++i) {
+    r = make_map(&maps[i], w[i], (long long)p.g[i].rows * a->n_layers,
+                 (long long)p.g[i].k_tiles * 64, (long long)p.g[i].k_tiles * 64, 128);
+    if (r) return r;
+  }
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(expert_step_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES) != cudaSuccess)
+      return fail(FVB_ERR_CUDA, "expert smem attribute: %s",
+                  cudaGetErrorString(cudaGetLastError()));
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeCooperative;
+  attrs[0].val.cooperative = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, expert_step_kernel, maps[0], maps[1],
+                                     maps[2], maps[3], p);
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "fvb_expert_step: launch failed: %s",
+                cudaGetErrorString(e));
+  return check_launch("fvb_expert_step");
+}
 
 // ---------------------------------------------------------------------------
 // Allocation-free attention.

@@ -72,8 +72,13 @@ class PI0EngineB200:
     """
 
     def __init__(self, cfg: PI0Config, weights: Dict[str, torch.Tensor],
-                 prefix_len: int, device='cuda', attn_splits: int = 0):
+                 prefix_len: int, device='cuda', attn_splits: int = 0,
+                 loop_impl: str = 'mega'):
         self.cfg = cfg
+        # 'mega': one persistent cooperative kernel per denoise step for all
+        # expert layers (fvb_expert_step); 'ops': one launch per operator
+        assert loop_impl in ('mega', 'ops')
+        self.loop_impl = loop_impl
         self.dev = torch.device(device)
         self.E = prefix_len
         self.S = cfg.n_suffix
@@ -143,6 +148,15 @@ class PI0EngineB200:
             elif pre + 'norm_dense_w' in W:
                 P[pre + 'norm_dense_w'] = W[pre + 'norm_dense_w']
                 P[pre + 'norm_dense_b'] = f32(W[pre + 'norm_dense_b'])
+        # layer-stacked expert weights (one tensor map per kind for the
+        # persistent step kernel); the per-layer entries become views
+        L = cfg.exp_layers
+        for n in ['qkv', 'o_w', 'gu', 'down_w']:
+            st = torch.cat([P[f'exp.l{i}.{n}'] for i in range(L)]).contiguous()
+            rows = st.shape[0] // L
+            P[f'exp.{n}_all'] = st
+            for i in range(L):
+                P[f'exp.l{i}.{n}'] = st[i * rows:(i + 1) * rows]
         for n in ['action_in', 'action_out', 'state_proj', 'action_time_in',
                   'action_time_out', 'time_in', 'time_out']:
             if n + '_w' in W:
@@ -240,8 +254,68 @@ class PI0EngineB200:
                 ops.small_linear(cond, P[nm + '_dense_w'], out,
                                  bias=P[nm + '_dense_b'])
                 self.mods[nm] = out
+        self._build_step_tables()
         if d.type == 'cuda':
             torch.cuda.synchronize(d)
+
+    def _build_step_tables(self):
+        """Per-step inputs of the persistent expert kernel.  RMSNorm enters
+        the GEMMs as x*(1+w) (rstd is applied by the consumer); adaRMSNorm as
+        x*(1+scale) plus the step-constant W*shift (bias) and the residual
+        gates (condition_gemma.py:118-147, 319-337)."""
+        cfg, P, B, d = self.cfg, self.P, self.B, self.dev
+        L, We = cfg.exp_layers, cfg.exp_width
+        hd, H = cfg.head_dim, cfg.heads
+        n = len(self.times)
+        if not cfg.adarms:
+            ins = torch.stack([1.0 + P[f'exp.l{i}.in_norm'].float()
+                               for i in range(L)]).contiguous()
+            posts = torch.stack([1.0 + P[f'exp.l{i}.post_norm'].float()
+                                 for i in range(L)]).contiguous()
+            self.step_tables = [dict(in_scale=ins, post_scale=posts)] * n
+            return
+        tabs = []
+        shift_in = torch.stack([self.mods[f'exp.l{i}.in_norm'][:, We:2 * We]
+                                for i in range(L)])        # [L, n, We]
+        shift_post = torch.stack([self.mods[f'exp.l{i}.post_norm'][:, We:2 * We]
+                                  for i in range(L)])
+        qkv_b = torch.empty(L, n, (H + 2) * hd, dtype=F32, device=d)
+        gu_b = torch.empty(L, n, 2 * cfg.exp_mlp, dtype=F32, device=d)
+        for i in range(L):
+            ops.small_linear(shift_in[i].contiguous(), P[f'exp.l{i}.qkv'],
+                             qkv_b[i])
+            ops.small_linear(shift_post[i].contiguous(), P[f'exp.l{i}.gu'],
+                             gu_b[i])
+        for k in range(n):
+            tabs.append(dict(
+                in_scale=torch.stack([1.0 + self.mods[f'exp.l{i}.in_norm'][k, :We]
+                                      for i in range(L)]).contiguous(),
+                post_scale=torch.stack([1.0 + self.mods[f'exp.l{i}.post_norm'][k, :We]
+                                        for i in range(L)]).contiguous(),
+                o_gate=torch.stack([self.mods[f'exp.l{i}.in_norm'][k, 2 * We:]
+                                    for i in range(L)]).contiguous(),
+                down_gate=torch.stack([self.mods[f'exp.l{i}.post_norm'][k, 2 * We:]
+                                       for i in range(L)]).contiguous(),
+                qkv_bias=qkv_b[:, k].contiguous(),
+                gu_bias=gu_b[:, k].contiguous()))
+        self.step_tables = tabs
+
+    def _expert_args(self, k: int):
+        cfg, P, B = self.cfg, self.P, self.B
+        a = dict(n_layers=cfg.exp_layers, n_tok=self.S, width=cfg.exp_width,
+                 mlp=cfg.exp_mlp, heads=cfg.heads, head_dim=cfg.head_dim,
+                 n_prefix=self.E, w_qkv=P['exp.qkv_all'], w_o=P['exp.o_w_all'],
+                 w_gu=P['exp.gu_all'], w_down=P['exp.down_w_all'],
+                 x=B['e_res'], k_cache=B['kc'], v_cache=B['vc'],
+                 key_valid=B['key_valid'], blocks=B['blocks'],
+                 positions=B['pos_suffix'], rope_cs=B['rope'])
+        a.update(self.step_tables[k])
+        if 'expert_ws' not in B:
+            nbytes = ops.expert_workspace_bytes(ops.expert_args(**a))
+            B['expert_ws'] = torch.zeros(nbytes, dtype=torch.uint8,
+                                         device=self.dev)
+        a['workspace'] = B['expert_ws']
+        return ops.expert_args(**a)
 
     # ------------------------------------------------------------------
     # prefix
@@ -343,6 +417,26 @@ class PI0EngineB200:
                      bias=P['action_time_out_b'], split_k=0)
             if off:
                 res[:off].copy_(B['state_emb'])
+        if self.loop_impl == 'mega':
+            ops.expert_step(self._expert_args(k))
+        else:
+            self._expert_layers_ops(k)
+        fin = B['e_fin'][off:]
+        if ada:
+            ops.norm(NORM_ADA_RMS, res[off:], fin, mod=self.mods['exp.norm'][k])
+        else:
+            ops.norm(NORM_GEMMA_RMS, res[off:], fin, w=P['exp.norm'])
+        # v_t = action_out_proj(out); x_t += dt * v_t (pi0_flowmatching.py:646)
+        ops.small_linear(fin, P['action_out_w'], B['x_t'],
+                         bias=P['action_out_b'], mode=2, alpha=self.dt)
+
+    def _expert_layers_ops(self, k: int):
+        """The expert layers with one launch per operator (reference path
+        for the persistent kernel)."""
+        cfg, P, B, E, S = self.cfg, self.P, self.B, self.E, self.S
+        hd, H, We = cfg.head_dim, cfg.heads, cfg.exp_width
+        ada = cfg.adarms
+        res = B['e_res']
         def attn(kc, vc):
             return ops.attn_args(
                 B['e_q'], kc, vc, B['e_ao'], n_q=S, n_kv=E + S, heads=H,
@@ -379,14 +473,6 @@ class PI0EngineB200:
             ops.gemm(P[p + 'down_w'], B['e_h'], res, swap=True,
                      epilogue=EPI_F32_ACC, split_k=0,
                      gate=m_post[2 * We:] if ada else None)
-        fin = B['e_fin'][off:]
-        if ada:
-            ops.norm(NORM_ADA_RMS, res[off:], fin, mod=self.mods['exp.norm'][k])
-        else:
-            ops.norm(NORM_GEMMA_RMS, res[off:], fin, w=P['exp.norm'])
-        # v_t = action_out_proj(out); x_t += dt * v_t (pi0_flowmatching.py:646)
-        ops.small_linear(fin, P['action_out_w'], B['x_t'],
-                         bias=P['action_out_b'], mode=2, alpha=self.dt)
 
     def _loop(self):
         self.B['x_t'].copy_(self.B['noise'])

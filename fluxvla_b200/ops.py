@@ -12,7 +12,8 @@ import torch
 
 from . import _lib
 from ._lib import (ACT_NONE, EPI_BF16, EPI_F32_ACC, EPI_F32_STORE,
-                   EPI_GEGLU, EPI_QKV_ROPE, AttnArgs, GemmArgs, check)
+                   EPI_GEGLU, EPI_QKV_ROPE, AttnArgs, ExpertArgs, GemmArgs,
+                   check)
 
 BF16 = torch.bfloat16
 F32 = torch.float32
@@ -165,3 +166,35 @@ def device_status(reset: bool = False) -> int:
 
 def launch_count() -> int:
     return _lib.lib().fvb_launch_count()
+
+
+def expert_args(*, n_layers, n_tok, width, mlp, heads, head_dim, n_prefix,
+                w_qkv, w_o, w_gu, w_down, in_scale, post_scale, x, k_cache,
+                v_cache, blocks, positions, rope_cs, qkv_bias=None,
+                gu_bias=None, o_gate=None, down_gate=None, key_valid=None,
+                eps=1e-6, workspace=None) -> ExpertArgs:
+    return ExpertArgs(
+        n_layers=n_layers, n_tok=n_tok, width=width, mlp=mlp, heads=heads,
+        head_dim=head_dim, n_prefix=n_prefix, w_qkv=_ptr(w_qkv),
+        w_o=_ptr(w_o), w_gu=_ptr(w_gu), w_down=_ptr(w_down),
+        in_scale=_ptr(in_scale), post_scale=_ptr(post_scale),
+        qkv_bias=_ptr(qkv_bias), gu_bias=_ptr(gu_bias), o_gate=_ptr(o_gate),
+        down_gate=_ptr(down_gate), eps=eps, x=_ptr(x),
+        k_cache=_ptr(k_cache), v_cache=_ptr(v_cache),
+        cache_rows=k_cache.shape[1], key_valid=_ptr(key_valid),
+        blocks=_ptr(blocks), positions=_ptr(positions),
+        rope_cs=_ptr(rope_cs), workspace=_ptr(workspace),
+        workspace_bytes=0 if workspace is None else
+        workspace.numel() * workspace.element_size())
+
+
+def expert_workspace_bytes(args: ExpertArgs) -> int:
+    n = _lib.lib().fvb_expert_workspace_bytes(C.byref(args))
+    if n < 0:
+        check(1)
+    return int(n)
+
+
+def expert_step(args: ExpertArgs) -> None:
+    """All expert layers of one denoise step (one cooperative launch)."""
+    check(_lib.lib().fvb_expert_step(C.byref(args), _stream()))

@@ -169,6 +169,54 @@ int fvb_attention_combine(const fvb_attn_args* args, void* stream);
  * the GPU race on it.                                                      */
 int fvb_attention_noalloc(const fvb_attn_args* args, void* stream);
 
+typedef struct fvb_expert_args {
+  int32_t n_layers;  /* expert layers run by one call (<= 64)              */
+  int32_t n_tok;     /* suffix tokens (<= 64)                              */
+  int32_t width;     /* hidden size (multiple of 128)                      */
+  int32_t mlp;       /* MLP width (multiple of 64)                         */
+  int32_t heads;     /* query heads; one KV head                           */
+  int32_t head_dim;  /* 256                                                */
+  int32_t n_prefix;  /* cached prefix rows E                               */
+  /* layer-stacked bf16 weights, nn.Linear layout, rows packed as for
+   * fvb_gemm (QKV pair-interleaved q|k|v, gate/up interleaved):          */
+  const void* w_qkv;  /* [L*(heads+2)*head_dim, width] */
+  const void* w_o;    /* [L*width, heads*head_dim]     */
+  const void* w_gu;   /* [L*2*mlp, width]              */
+  const void* w_down; /* [L*width, mlp]                */
+  const float* in_scale;   /* [L, width]: 1 + w (RMS) or 1 + scale (adaRMS) */
+  const float* post_scale; /* [L, width]                                     */
+  const float* qkv_bias;   /* [L, (heads+2)*head_dim] W_qkv.shift or NULL    */
+  const float* gu_bias;    /* [L, 2*mlp] W_gu.shift or NULL                  */
+  const float* o_gate;     /* [L, width] residual gates or NULL (= 1)        */
+  const float* down_gate;  /* [L, width] or NULL                             */
+  float eps;
+  float* x;                /* f32 residual [n_tok, width], updated in place  */
+  const void* k_cache;     /* bf16 [L, cache_rows, head_dim]; rows < n_prefix
+                            * are read (the prefix KV cache)                 */
+  const void* v_cache;
+  int64_t cache_rows;
+  const uint8_t* key_valid;  /* [n_prefix] or NULL                          */
+  const int32_t* blocks;     /* [n_tok] suffix attention block ids (cumsum
+                              * of the att mask): key s visible to query t
+                              * iff blocks[s] <= blocks[t]                  */
+  const int32_t* positions;  /* [n_tok] RoPE positions                      */
+  const float* rope_cs;      /* [max_pos, head_dim/2, 2]                    */
+  void* workspace;           /* fvb_expert_workspace_bytes(); zero-filled
+                              * before the first call, left reusable        */
+  int64_t workspace_bytes;
+} fvb_expert_args;
+
+/* All layers of one flow-matching step of the action expert in ONE
+ * persistent cooperative kernel (one CTA per SM, grid barriers between the
+ * QKV / attention / merge / o_proj / gate-up / down phases; weights streamed
+ * by TMA across phase boundaries; tcgen05 MMAs with split-K f32
+ * accumulation).  Replaces the per-layer launches of transformer_decoder
+ * (fluxvla/models/vlas/pi05_flowmatching_inference.py:155-312: adarms_norm_
+ * style_proj, matmul_qkv_rope, matmul_abT_scale, softmax_kernel_prefix_suffix,
+ * matmul_attn_v, matmul_res_gate, matmul_gate) for PI0 and PI0.5.          */
+int fvb_expert_step(const fvb_expert_args* args, void* stream);
+int64_t fvb_expert_workspace_bytes(const fvb_expert_args* args);
+
 /* Row normalisation, f32 input rows [rows, dim] (row stride ld_in), output
  * bf16 or f32 (out_f32 != 0) with row stride ld_out.
  * mode FVB_NORM_GEMMA_RMS: w = bf16 [dim]; FVB_NORM_ADA_RMS: mod = f32

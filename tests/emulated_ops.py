@@ -164,6 +164,64 @@ def small_linear(x, w, out, *, bias=None, act=0, mode=0, alpha=1.0, k=None):
         out.copy_(y.to(out.dtype))
 
 
+def expert_args(**kw):
+    d = dict(qkv_bias=None, gu_bias=None, o_gate=None, down_gate=None,
+             key_valid=None, eps=1e-6, workspace=None)
+    d.update(kw)
+    return _Args(**d)
+
+
+def expert_workspace_bytes(args):
+    return 16
+
+
+def expert_step(a):
+    """Same factorisation as the persistent kernel: GEMMs on x*(1+w), the
+    per-token rstd applied by the consumer, adaRMS shift as W*shift bias."""
+    _count[0] += 1
+    L, S, W, hd, H = a.n_layers, a.n_tok, a.width, a.head_dim, a.heads
+    E, half = a.n_prefix, a.head_dim // 2
+    x = a.x
+    pos = a.positions.long()
+    c = a.rope_cs[pos, :, 0][:, None]
+    s = a.rope_cs[pos, :, 1][:, None]
+    blk = a.blocks[:S]
+    qkv_rows = (H + 2) * hd
+    for l in range(L):
+        wq = a.w_qkv[l * qkv_rows:(l + 1) * qkv_rows].float()
+        rs = torch.rsqrt((x * x).mean(-1, keepdim=True) + a.eps)
+        acc = (x * a.in_scale[l]) @ wq.t() * rs
+        if a.qkv_bias is not None:
+            acc = acc + a.qkv_bias[l]
+        qk = acc[:, :(H + 1) * hd].reshape(S, H + 1, half, 2)
+        x1, x2 = qk[..., 0], qk[..., 1]
+        r = torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1)
+        q, k = r[:, :H], r[:, H]
+        v = acc[:, (H + 1) * hd:]
+        kk = torch.cat([a.k_cache[l, :E].float(), k.bfloat16().float()])
+        vv = torch.cat([a.v_cache[l, :E].float(), v.bfloat16().float()])
+        mask = torch.ones(S, E + S, dtype=torch.bool)
+        if a.key_valid is not None:
+            mask[:, :E] &= a.key_valid[:E].bool()[None]
+        mask[:, E:] &= blk[None] <= blk[:, None]
+        att = torch.einsum('thd,kd->htk', q.bfloat16().float(), kk) * hd ** -0.5
+        att = att.masked_fill(~mask[None], float('-inf')).softmax(-1)
+        o = torch.einsum('htk,kd->thd', att, vv).reshape(S, H * hd)
+        wo = a.w_o[l * W:(l + 1) * W].float()
+        y = o.bfloat16().float() @ wo.t()
+        x += y * (a.o_gate[l] if a.o_gate is not None else 1)
+        rs = torch.rsqrt((x * x).mean(-1, keepdim=True) + a.eps)
+        gu_rows = 2 * a.mlp
+        wg = a.w_gu[l * gu_rows:(l + 1) * gu_rows].float()
+        gu = (x * a.post_scale[l]) @ wg.t() * rs
+        if a.gu_bias is not None:
+            gu = gu + a.gu_bias[l]
+        h = (F.gelu(gu[:, 0::2], approximate='tanh') * gu[:, 1::2]).bfloat16()
+        wd = a.w_down[l * W:(l + 1) * W].float()
+        y = h.float() @ wd.t()
+        x += y * (a.down_gate[l] if a.down_gate is not None else 1)
+
+
 def launch_count():
     return _count[0]
 
@@ -171,7 +229,8 @@ def launch_count():
 def install(monkeypatch):
     from fluxvla_b200 import engine, ops
     for name in ['gemm', 'attn_args', 'attention', 'attention_workspace_bytes',
-                 'gemm_workspace_bytes',
+                 'gemm_workspace_bytes', 'expert_args', 'expert_step',
+                 'expert_workspace_bytes',
                  'norm', 'patchify', 'embed_tokens', 'small_linear',
                  'launch_count']:
         monkeypatch.setattr(ops, name, globals()[name])

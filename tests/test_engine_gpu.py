@@ -35,8 +35,9 @@ def request(cfg, seed, n_tokens):
     return imgs, toks, state, noise
 
 
+@pytest.mark.parametrize('loop_impl', ['mega', 'ops'])
 @pytest.mark.parametrize('pi05', [False, True])
-def test_denoise_loop_external_cache(pi05):
+def test_denoise_loop_external_cache(pi05, loop_impl):
     """config[1] geometry (expert width 1024, 816-row prefix cache ~N(0,1),
     51 or 50 suffix tokens, 10 Euler steps) at reduced depth."""
     kw = dict(exp_layers=3, llm_layers=3)
@@ -49,7 +50,7 @@ def test_denoise_loop_external_cache(pi05):
           for _ in range(cfg.exp_layers)]
     state = torch.randn(1, cfg.state_dim, generator=g)
     noise = torch.randn(1, cfg.n_actions, cfg.action_dim, generator=g)
-    eng = PI0EngineB200(cfg, W, prefix_len=E)
+    eng = PI0EngineB200(cfg, W, prefix_len=E, loop_impl=loop_impl)
     eng.set_prefix_cache(torch.stack([k[0, 0] for k, _ in kv]),
                          torch.stack([v[0, 0] for _, v in kv]))
     eng.load_inputs(state=state, noise=noise)
