@@ -64,6 +64,7 @@ class ExpertArgs(C.Structure):
                 ('v_cache', C.c_void_p), ('cache_rows', C.c_int64),
                 ('key_valid', C.c_void_p), ('blocks', C.c_void_p),
                 ('positions', C.c_void_p), ('rope_cs', C.c_void_p),
+                ('rope_suffix', C.c_void_p),
                 ('workspace', C.c_void_p), ('workspace_bytes', C.c_int64)]
 
 
@@ -91,6 +92,7 @@ EXPORTS = {
                                    C.c_int32, C.c_float, C.c_void_p,
                                    C.c_int64, C.c_void_p]),
     'fvb_gemm_trace_next': (C.c_int, []),
+    'fvb_expert_trace_read': (C.c_int, [C.c_void_p, C.c_int32]),
     'fvb_gemm_trace_read': (C.c_int, [C.c_void_p, C.c_int32]),
     'fvb_get_device_status': (C.c_int, [C.POINTER(C.c_int), C.c_int]),
     'fvb_last_error': (C.c_char_p, []),

@@ -69,6 +69,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `hint_ns`
+// while the phase is incomplete, so a waiting role does not keep issuing
+// instructions next to the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t addr,
+                                                    uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Returns false (and
 // records a device error) if it does not complete within FVB_WAIT_LIMIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
@@ -76,8 +93,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(addr, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(addr, parity, 20000)) return true;
     if (globaltimer_ns() - t0 > FVB_WAIT_LIMIT_NS) {
       record_device_error(FVB_ERR_DEVICE_TIMEOUT);
       return false;
@@ -97,6 +114,28 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst,
       "bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
       "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Streaming variant: the tile is read once, so it should not displace the
+// activations that stay resident in L2 (evict-first cache policy).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void tma_load_2d_stream(void* smem_dst,
+                                                   const CUtensorMap* map,
+                                                   int32_t x, int32_t y,
+                                                   uint64_t* bar,
+                                                   uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+      "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 

@@ -39,7 +39,7 @@ constexpr int BKT_BYTES = TOK * 64 * 2;    // B k-tile (8 KB)
 constexpr int MAX_KT = 8;                  // k-tiles per work item
 constexpr int APITCH = 264;                // attention smem row pitch (bf16)
 constexpr int ATILE = 64 * APITCH;         // elements per attention tile
-constexpr int REGION_BYTES = 3 * ATILE * 2 + 64 + 64 * 4;  // >= MAX_KT*BKT
+constexpr int REGION_BYTES = 3 * ATILE * 2 + 64 + 64 * 4 + 2 * 64 * 4;  // >= MAX_KT*BKT
 constexpr int SMEM_BYTES = 1024 + STAGES * A_BYTES + REGION_BYTES + 256;
 constexpr int N_GEMM = 4;  // QKV, O, GU, DOWN
 
@@ -70,6 +70,7 @@ struct Params {
   const int* blocks;
   const int* positions;
   const float* rope_cs;
+  const float* rope_suf;    // [n_tok, hd/2, 2] cos/sin at the suffix positions
   float scale_log2;
   // workspace
   float* acc_qkv;  // [TOK, (H+2)*hd]
@@ -79,20 +80,30 @@ struct Params {
   float* part_o;   // [heads*nkb, TOK, hd]
   float* part_ml;  // [heads*nkb, TOK, 2]
   bf16* attn;      // [TOK, heads*hd]
+  bf16* qb;        // [TOK, heads*hd] rotated queries (rows >= n_tok zero)
+  bf16* xs;        // [TOK, width] x*(1+w) for the QKV / gate-up B operand
+  bf16* hb;        // [TOK, mlp] gelu(g)*u for the down B operand
+  bf16* kvs;       // [2][128, hd] suffix keys (rotated) / values (rows >= n_tok zero)
   unsigned* bar;   // [0] count, [1] generation, [2] abort
   int nkb;         // key blocks of 64
+  int trace;       // diagnostics: phase stamps of layer 0 in g_mega_trace
+  int stages;      // weight ring depth in use (<= STAGES)
 };
+
+// Diagnostics: per CTA, globaltimer at worker start, then after the work
+// and after the barrier of each of the 6 phases of layer 0.
+__device__ unsigned long long g_mega_trace[256][32];
 
 // ---------------------------------------------------------------------------
 // waits with a time limit and a shared abort flag
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ bool aborted(const Params& p) {
-  return *reinterpret_cast<volatile unsigned*>(p.bar + 2) != 0u;
+  return *reinterpret_cast<volatile unsigned*>(p.bar + 288) != 0u;
 }
 
 __device__ __forceinline__ void set_abort(const Params& p) {
   record_device_error(FVB_ERR_DEVICE_TIMEOUT);
-  atomicExch(p.bar + 2, 1u);
+  atomicExch(p.bar + 288, 1u);
 }
 
 __device__ __forceinline__ bool wait_bar(const Params& p, uint64_t* bar,
@@ -101,8 +112,8 @@ __device__ __forceinline__ bool wait_bar(const Params& p, uint64_t* bar,
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(addr, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(addr, parity, 20000)) return true;
     if (aborted(p)) return false;
     if (globaltimer_ns() - t0 > FVB_WAIT_LIMIT_NS) {
       set_abort(p);
@@ -115,28 +126,39 @@ __device__ __forceinline__ void bar128() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-// Grid barrier among the 4 worker warps of every CTA.
+// Grid barrier among the 4 worker warps of every CTA: one acquire-release
+// arrival counter (bar[0]), a generation word (bar[BAR_GEN]) polled with
+// acquire loads, and the abort flag (bar[BAR_ABORT]) on its own line.
+constexpr int BAR_GEN = 32, BAR_ABORT = 288, BAR_WORDS = 320;
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* a, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old) : "l"(a), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void grid_sync(const Params& p, int wtid) {
-  __threadfence();
   bar128();
   if (wtid == 0) {
-    volatile unsigned* gen = p.bar + 1;
-    const unsigned g = *gen;
-    if (atomicAdd(p.bar, 1u) == gridDim.x - 1) {
-      p.bar[0] = 0u;
-      __threadfence();
-      atomicAdd(p.bar + 1, 1u);
-    } else {
-      const uint64_t t0 = globaltimer_ns();
-      while (*gen == g) {
+    // bar[0] only grows: the k-th barrier of the kernel's history completes
+    // when it reaches (k+1)*gridDim.x, and each arrival learns k from the
+    // value it replaced
+    const unsigned G = gridDim.x;
+    const unsigned old = atom_add_acq_rel(p.bar, 1u);
+    const unsigned target = (old / G + 1) * G;
+    uint64_t t0 = 0;
+    for (unsigned n = 0; (int)(ld_acquire(p.bar) - target) < 0; ++n) {
+      if ((n & 255) == 255) {
         if (aborted(p)) break;
-        if (globaltimer_ns() - t0 > FVB_WAIT_LIMIT_NS) {
-          set_abort(p);
-          break;
-        }
+        const uint64_t now = globaltimer_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > FVB_WAIT_LIMIT_NS) { set_abort(p); break; }
       }
     }
-    __threadfence();
   }
   bar128();
 }
@@ -156,136 +178,10 @@ __device__ __forceinline__ int b_off(int t, int kc) {
 }
 
 // ---------------------------------------------------------------------------
-// B operand builders (worker warps, 128 threads)
-// ---------------------------------------------------------------------------
-// The builders walk 16-byte B chunks (token t, 8 consecutive k) with the
-// chunk index fastest along k, four chunks per thread per round: the global
-// loads of a round are all issued before any of them is used.
-constexpr int BATCH = 4;
-
-// B[t,k] = x[t,k]*scale[k] for k in [k0, k0 + nkt*64); optional sum of x^2
-__device__ void build_b_scaled(const Params& p, uint8_t* B, const float* x,
-                               int ldx, const float* scale, int k0, int nkt,
-                               float* ss, int wtid) {
-  const int nch = nkt * 8, total = TOK * nch;
-  for (int base = wtid; base < total; base += 128 * BATCH) {
-    float4 a[BATCH], b[BATCH];
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int c = base + u * 128;
-      const int t = c / nch, kc = c % nch;
-      a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c < total && t < p.n_tok) {
-        const float* src = x + (long long)t * ldx + k0 + kc * 8;
-        a[u] = ldcg4(src);
-        b[u] = ldcg4(src + 4);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int c = base + u * 128;
-      if (c >= total) break;
-      const int t = c / nch, kc = c % nch;
-      uint4 w = make_uint4(0, 0, 0, 0);
-      if (t < p.n_tok) {
-        const int k = k0 + kc * 8;
-        const float4 sa = __ldg(reinterpret_cast<const float4*>(scale + k));
-        const float4 sb = __ldg(reinterpret_cast<const float4*>(scale + k + 4));
-        w = make_uint4(pack_bf16x2(a[u].x * sa.x, a[u].y * sa.y),
-                       pack_bf16x2(a[u].z * sa.z, a[u].w * sa.w),
-                       pack_bf16x2(b[u].x * sb.x, b[u].y * sb.y),
-                       pack_bf16x2(b[u].z * sb.z, b[u].w * sb.w));
-        if (ss) {
-          const float q = a[u].x * a[u].x + a[u].y * a[u].y + a[u].z * a[u].z +
-                          a[u].w * a[u].w + b[u].x * b[u].x + b[u].y * b[u].y +
-                          b[u].z * b[u].z + b[u].w * b[u].w;
-          atomicAdd(ss + t, q);
-        }
-      }
-      *reinterpret_cast<uint4*>(B + b_off(t, kc)) = w;
-    }
-  }
-}
-
-// B[t,k] = attn[t,k] (bf16 copy)
-__device__ void build_b_copy(const Params& p, uint8_t* B, const bf16* src,
-                             int lds, int k0, int nkt, int wtid) {
-  const int nch = nkt * 8, total = TOK * nch;
-  for (int base = wtid; base < total; base += 128 * BATCH) {
-    uint4 w[BATCH];
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int c = base + u * 128;
-      const int t = c / nch, kc = c % nch;
-      w[u] = make_uint4(0, 0, 0, 0);
-      if (c < total && t < p.n_tok)
-        w[u] = __ldcg(reinterpret_cast<const uint4*>(src + (long long)t * lds + k0 + kc * 8));
-    }
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int c = base + u * 128;
-      if (c >= total) break;
-      *reinterpret_cast<uint4*>(B + b_off(c / nch, c % nch)) = w[u];
-    }
-  }
-}
-
-// B[t,i] = gelu(rs*g + bg) * (rs*u + bu), (g, u) = acc_gu[t, 2i], [t, 2i+1]
-__device__ void build_b_geglu(const Params& p, uint8_t* B, const float* gub,
-                              int k0, int nkt, int wtid) {
-  const int nch = nkt * 8, total = TOK * nch;
-  const int ld = 2 * p.mlp;
-  for (int base = wtid; base < total; base += 128 * 2) {
-    float4 q[2][4];
-    float rs[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int c = base + u * 128;
-      const int t = c / nch, kc = c % nch;
-      rs[u] = 0.f;
-#pragma unroll
-      for (int h = 0; h < 4; ++h) q[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c < total && t < p.n_tok) {
-        rs[u] = __ldcg(p.ss_post + t);
-        const float* src = p.acc_gu + (long long)t * ld + 2 * (k0 + kc * 8);
-#pragma unroll
-        for (int h = 0; h < 4; ++h) q[u][h] = ldcg4(src + 4 * h);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int c = base + u * 128;
-      if (c >= total) break;
-      const int t = c / nch, kc = c % nch;
-      uint4 w = make_uint4(0, 0, 0, 0);
-      if (t < p.n_tok) {
-        const float r = rsqrtf(rs[u] / p.width + p.eps);
-        const int i0 = k0 + kc * 8;
-        float y[8];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float g0 = r * q[u][h].x, u0 = r * q[u][h].y;
-          float g1 = r * q[u][h].z, u1 = r * q[u][h].w;
-          if (gub) {
-            const float4 bq = __ldg(reinterpret_cast<const float4*>(gub + 2 * i0 + 4 * h));
-            g0 += bq.x; u0 += bq.y; g1 += bq.z; u1 += bq.w;
-          }
-          y[2 * h] = gelu_tanh_f(g0) * u0;
-          y[2 * h + 1] = gelu_tanh_f(g1) * u1;
-        }
-        w = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
-                       pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
-      }
-      *reinterpret_cast<uint4*>(B + b_off(t, kc)) = w;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
 // attention block: 64 query rows (one head) x one 64-key block
 // ---------------------------------------------------------------------------
 __device__ void attention_item(const Params& p, int layer, int item,
-                               uint8_t* region, int wtid) {
+                               uint8_t* region, int wtid, bool tr) {
   const int H = p.heads, hd = p.hd, half = hd >> 1;
   const int h = item / p.nkb, kb = item % p.nkb;
   const int S = p.n_tok, E = p.n_prefix, n_kv = E + S;
@@ -299,104 +195,25 @@ __device__ void attention_item(const Params& p, int layer, int item,
   const bf16* kc = p.kc + layer * p.cache_layer;
   const bf16* vc = p.vc + layer * p.cache_layer;
 
-  // prefix keys of this block: cp.async from the bf16 cache
+  // operands: rotated queries of head h, prefix keys/values from the cache,
+  // suffix keys/values from the finalized buffers; rows past the end zero
   const int key0 = kb * 64;
+  const bf16* ks = p.kvs;
+  const bf16* vs = p.kvs + 128 * hd;
   for (int c = wtid; c < 64 * (hd / 8); c += 128) {
     const int r = c / (hd / 8), cc = c % (hd / 8);
+    cp_async16(sQ + r * APITCH + cc * 8,
+               p.qb + (long long)r * H * hd + h * hd + cc * 8, true);
     const int key = key0 + r;
-    // rows past the prefix are written by the suffix build below (no async
-    // copy may target them)
-    if (key < E) {
-      cp_async16(sK + r * APITCH + cc * 8, kc + (long long)key * hd + cc * 8, true);
-      cp_async16(sV + r * APITCH + cc * 8, vc + (long long)key * hd + cc * 8, true);
-    }
+    const bool pre = key < E;
+    const int sr = key - E;
+    const bool suf = !pre && sr < 128;
+    const bf16* kk = pre ? kc + (long long)key * hd : (suf ? ks + sr * hd : ks);
+    const bf16* vv = pre ? vc + (long long)key * hd : (suf ? vs + sr * hd : vs);
+    cp_async16(sK + r * APITCH + cc * 8, kk + cc * 8, pre || suf);
+    cp_async16(sV + r * APITCH + cc * 8, vv + cc * 8, pre || suf);
   }
   cp_async_commit();
-  // queries (and the suffix keys/values of this block) from the QKV
-  // accumulator: rows t x rotary pairs i, four per thread per round
-  for (int base = wtid; base < 64 * half; base += 128 * BATCH) {
-    float2 a[BATCH], cs[BATCH];
-    float rs[BATCH];
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int c = base + u * 128;
-      const int t = c / half, i = c % half;
-      a[u] = cs[u] = make_float2(0.f, 0.f);
-      rs[u] = 0.f;
-      if (c < 64 * half && t < S) {
-        rs[u] = __ldcg(p.ss_in + t);
-        a[u] = __ldcg(reinterpret_cast<const float2*>(
-            p.acc_qkv + (long long)t * qkv_ld + h * hd + 2 * i));
-        cs[u] = *reinterpret_cast<const float2*>(
-            p.rope_cs + ((long long)p.positions[t] * half + i) * 2);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int c = base + u * 128;
-      if (c >= 64 * half) break;
-      const int t = c / half, i = c % half;
-      float q1 = 0.f, q2 = 0.f;
-      if (t < S) {
-        const float r = rsqrtf(rs[u] / p.width + p.eps);
-        float x1 = r * a[u].x, x2 = r * a[u].y;
-        if (bias) { x1 += bias[h * hd + 2 * i]; x2 += bias[h * hd + 2 * i + 1]; }
-        q1 = x1 * cs[u].x - x2 * cs[u].y;
-        q2 = x2 * cs[u].x + x1 * cs[u].y;
-      }
-      sQ[t * APITCH + i] = __float2bfloat16(q1);
-      sQ[t * APITCH + i + half] = __float2bfloat16(q2);
-    }
-  }
-  const int r_suf = max(0, E - key0);  // first row of this block past the prefix
-  if (r_suf < 64) {
-    const int nrow = 64 - r_suf;
-    for (int base = wtid; base < nrow * half; base += 128 * BATCH) {
-      float2 a[BATCH], cs[BATCH];
-      float vv[BATCH][2], rs[BATCH];
-#pragma unroll
-      for (int u = 0; u < BATCH; ++u) {
-        const int c = base + u * 128;
-        const int r = r_suf + c / half, i = c % half;
-        const int key = key0 + r;
-        a[u] = cs[u] = make_float2(0.f, 0.f);
-        vv[u][0] = vv[u][1] = rs[u] = 0.f;
-        if (c < nrow * half && key < n_kv) {
-          const int s = key - E;
-          const float* row = p.acc_qkv + (long long)s * qkv_ld;
-          rs[u] = __ldcg(p.ss_in + s);
-          a[u] = __ldcg(reinterpret_cast<const float2*>(row + H * hd + 2 * i));
-          vv[u][0] = __ldcg(row + (H + 1) * hd + i);
-          vv[u][1] = __ldcg(row + (H + 1) * hd + i + half);
-          cs[u] = *reinterpret_cast<const float2*>(
-              p.rope_cs + ((long long)p.positions[s] * half + i) * 2);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < BATCH; ++u) {
-        const int c = base + u * 128;
-        if (c >= nrow * half) break;
-        const int r = r_suf + c / half, i = c % half;
-        float k1 = 0.f, k2 = 0.f, v1 = 0.f, v2 = 0.f;
-        if (key0 + r < n_kv) {
-          const float rr = rsqrtf(rs[u] / p.width + p.eps);
-          float x1 = rr * a[u].x, x2 = rr * a[u].y;
-          v1 = rr * vv[u][0];
-          v2 = rr * vv[u][1];
-          if (bias) {
-            x1 += bias[H * hd + 2 * i]; x2 += bias[H * hd + 2 * i + 1];
-            v1 += bias[(H + 1) * hd + i]; v2 += bias[(H + 1) * hd + i + half];
-          }
-          k1 = x1 * cs[u].x - x2 * cs[u].y;
-          k2 = x2 * cs[u].x + x1 * cs[u].y;
-        }
-        sK[r * APITCH + i] = __float2bfloat16(k1);
-        sK[r * APITCH + i + half] = __float2bfloat16(k2);
-        sV[r * APITCH + i] = __float2bfloat16(v1);
-        sV[r * APITCH + i + half] = __float2bfloat16(v2);
-      }
-    }
-  }
   if (wtid < 64) {
     const int key = key0 + wtid;
     uint8_t vis = key < n_kv;
@@ -517,32 +334,190 @@ __device__ void attention_item(const Params& p, int layer, int item,
   bar128();  // the region is reused by the next item
 }
 
-// merge of the key-block partials of one (head, token) row -> attn (bf16)
-__device__ void combine_row(const Params& p, int row, int wtid) {
-  const int S = p.n_tok, hd = p.hd;
-  const int h = row / S, t = row % S;
-  float M = -INFINITY;
-  for (int kb = 0; kb < p.nkb; ++kb) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(
-        p.part_ml + ((long long)(h * p.nkb + kb) * TOK + t) * 2));
-    if (ml.y > 0.f) M = fmaxf(M, ml.x);
+// xs[t,k] = bf16(x[t,k]*scale[k]) and ss[t] += sum_k x[t,k]^2, spread over
+// the grid (8 values per thread; a warp covers 256 values of one token)
+__device__ void prep_scaled(const Params& p, const float* scale, float* ss,
+                            int wtid) {
+  const int per_tok = p.width / 8;
+  const int total = p.n_tok * per_tok;
+  const int lane = wtid & 31;
+  for (int c = blockIdx.x * 128 + wtid; c - lane < total; c += gridDim.x * 128) {
+    float q = 0.f;
+    int t = 0;
+    if (c < total) {
+      t = c / per_tok;
+      const int k = (c % per_tok) * 8;
+      const float4 a = ldcg4(p.x + (long long)t * p.width + k);
+      const float4 b = ldcg4(p.x + (long long)t * p.width + k + 4);
+      const float4 sa = __ldg(reinterpret_cast<const float4*>(scale + k));
+      const float4 sb = __ldg(reinterpret_cast<const float4*>(scale + k + 4));
+      *reinterpret_cast<uint4*>(p.xs + (long long)t * p.width + k) =
+          make_uint4(pack_bf16x2(a.x * sa.x, a.y * sa.y),
+                     pack_bf16x2(a.z * sa.z, a.w * sa.w),
+                     pack_bf16x2(b.x * sb.x, b.y * sb.y),
+                     pack_bf16x2(b.z * sb.z, b.w * sb.w));
+      q = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x +
+          b.y * b.y + b.z * b.z + b.w * b.w;
+    }
+    q = warp_sum(q);  // per_tok is a multiple of 32: one token per warp
+    if (lane == 0 && c < total) atomicAdd(ss + t, q);
   }
-  float L = 0.f, acc0 = 0.f, acc1 = 0.f;
-  const int d = wtid * 2;
-  for (int kb = 0; kb < p.nkb; ++kb) {
-    const long long it = h * p.nkb + kb;
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (it * TOK + t) * 2));
-    if (ml.y > 0.f) {
-      const float w = exp2f(ml.x - M);
-      L += w * ml.y;
-      const float2 o = __ldcg(reinterpret_cast<const float2*>(p.part_o + (it * TOK + t) * hd + d));
-      acc0 += w * o.x;
-      acc1 += w * o.y;
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// hb[t,i] = bf16(gelu(rs*g + bg) * (rs*u + bu)), (g,u) = acc_gu[t, 2i..2i+1]
+__device__ void prep_geglu(const Params& p, const float* gub, int wtid) {
+  const int per_tok = p.mlp / 8;
+  const int total = p.n_tok * per_tok;
+  const int ld = 2 * p.mlp;
+  constexpr int PB = 2;
+  for (int base = blockIdx.x * 128 + wtid; base < total; base += gridDim.x * 128 * PB) {
+    float4 q[PB][4];
+    float rs[PB];
+#pragma unroll
+    for (int u = 0; u < PB; ++u) {
+      const int c = base + u * gridDim.x * 128;
+      rs[u] = 0.f;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) q[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < total) {
+        const int t = c / per_tok, i0 = (c % per_tok) * 8;
+        rs[u] = __ldcg(p.ss_post + t);
+        const float* src = p.acc_gu + (long long)t * ld + 2 * i0;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) q[u][h] = ldcg4(src + 4 * h);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < PB; ++u) {
+      const int c = base + u * gridDim.x * 128;
+      if (c >= total) break;
+      const int t = c / per_tok, i0 = (c % per_tok) * 8;
+      const float r = rsqrtf(rs[u] / p.width + p.eps);
+      float y[8];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float g0 = r * q[u][h].x, u0 = r * q[u][h].y;
+        float g1 = r * q[u][h].z, u1 = r * q[u][h].w;
+        if (gub) {
+          const float4 bq = __ldg(reinterpret_cast<const float4*>(gub + 2 * i0 + 4 * h));
+          g0 += bq.x; u0 += bq.y; g1 += bq.z; u1 += bq.w;
+        }
+        y[2 * h] = gelu_tanh_f(g0) * u0;
+        y[2 * h + 1] = gelu_tanh_f(g1) * u1;
+      }
+      *reinterpret_cast<uint4*>(p.hb + (long long)t * p.mlp + i0) =
+          make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                     pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
     }
   }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  *reinterpret_cast<uint32_t*>(p.attn + (long long)t * p.heads * hd + h * hd + d) =
-      pack_bf16x2(acc0 * inv, acc1 * inv);
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// q = rope(rstd*acc_q + b), k = rope(rstd*acc_k + b), v = rstd*acc_v + b for
+// the suffix tokens, written once as bf16 for every attention item.
+// Task (t, i): i < (H+1)*hd/2 is a rotary pair of a query head or the key
+// head, otherwise a pair (d, d + hd/2) of the value head.
+__device__ void finalize_qkv(const Params& p, int layer, int wtid) {
+  const int H = p.heads, hd = p.hd, half = hd >> 1;
+  const int qkv_ld = (H + 2) * hd;
+  const int per_tok = (H + 2) * half;
+  const int total = p.n_tok * per_tok;
+  const float* bias = p.qkv_bias ? p.qkv_bias + (long long)layer * qkv_ld : nullptr;
+  constexpr int FB = 4;
+  for (int base = blockIdx.x * 128 + wtid; base < total; base += gridDim.x * 128 * FB) {
+    float2 a[FB], cs[FB];
+    float rs[FB];
+#pragma unroll
+    for (int u = 0; u < FB; ++u) {
+      const int c = base + u * gridDim.x * 128;
+      a[u] = cs[u] = make_float2(0.f, 0.f);
+      rs[u] = 0.f;
+      if (c < total) {
+        const int t = c / per_tok, i = c % per_tok;
+        const float* row = p.acc_qkv + (long long)t * qkv_ld;
+        rs[u] = __ldcg(p.ss_in + t);
+        if (i < (H + 1) * half) {
+          const int hh = i / half, ii = i % half;
+          a[u] = __ldcg(reinterpret_cast<const float2*>(row + hh * hd + 2 * ii));
+          cs[u] = __ldg(reinterpret_cast<const float2*>(
+              p.rope_suf + ((long long)t * half + ii) * 2));
+        } else {
+          const int d = i - (H + 1) * half;
+          a[u].x = __ldcg(row + (H + 1) * hd + d);
+          a[u].y = __ldcg(row + (H + 1) * hd + d + half);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < FB; ++u) {
+      const int c = base + u * gridDim.x * 128;
+      if (c >= total) break;
+      const int t = c / per_tok, i = c % per_tok;
+      const float r = rsqrtf(rs[u] / p.width + p.eps);
+      if (i < (H + 1) * half) {
+        const int hh = i / half, ii = i % half;
+        float x1 = r * a[u].x, x2 = r * a[u].y;
+        if (bias) { x1 += bias[hh * hd + 2 * ii]; x2 += bias[hh * hd + 2 * ii + 1]; }
+        const float o1 = x1 * cs[u].x - x2 * cs[u].y;
+        const float o2 = x2 * cs[u].x + x1 * cs[u].y;
+        bf16* dst = hh < H ? p.qb + (long long)t * H * hd + hh * hd : p.kvs + t * hd;
+        dst[ii] = __float2bfloat16(o1);
+        dst[ii + half] = __float2bfloat16(o2);
+      } else {
+        const int d = i - (H + 1) * half;
+        float v1 = r * a[u].x, v2 = r * a[u].y;
+        if (bias) { v1 += bias[(H + 1) * hd + d]; v2 += bias[(H + 1) * hd + d + half]; }
+        bf16* dst = p.kvs + 128 * hd + t * hd;
+        dst[d] = __float2bfloat16(v1);
+        dst[d + half] = __float2bfloat16(v2);
+      }
+    }
+  }
+}
+
+// merge of the key-block partials of one (head, token) row -> attn (bf16)
+constexpr int MAX_NKB = 16;
+// merge of the key-block partials: task (head, token, 4 dims), spread over
+// the whole grid
+__device__ void merge_partials(const Params& p, int wtid) {
+  const int S = p.n_tok, hd = p.hd;
+  const int quads = hd / 4;
+  const int total = p.heads * S * quads;
+  for (int c = blockIdx.x * 128 + wtid; c < total; c += gridDim.x * 128) {
+    const int row = c / quads, d = (c % quads) * 4;
+    const int h = row / S, t = row % S;
+    float2 ml[MAX_NKB];
+    float4 o[MAX_NKB];
+#pragma unroll
+    for (int kb = 0; kb < MAX_NKB; ++kb) {
+      ml[kb] = make_float2(-INFINITY, 0.f);
+      o[kb] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (kb < p.nkb) {
+        const long long it = h * p.nkb + kb;
+        ml[kb] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (it * TOK + t) * 2));
+        o[kb] = ldcg4(p.part_o + (it * TOK + t) * hd + d);
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int kb = 0; kb < MAX_NKB; ++kb)
+      if (ml[kb].y > 0.f) M = fmaxf(M, ml[kb].x);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int kb = 0; kb < MAX_NKB; ++kb) {
+      if (ml[kb].y > 0.f) {
+        const float w = exp2f(ml[kb].x - M);
+        L += w * ml[kb].y;
+        acc.x += w * o[kb].x; acc.y += w * o[kb].y;
+        acc.z += w * o[kb].z; acc.w += w * o[kb].w;
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    *reinterpret_cast<uint2*>(p.attn + (long long)t * p.heads * hd + h * hd + d) =
+        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -553,6 +528,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                        const __grid_constant__ CUtensorMap tm_o,
                        const __grid_constant__ CUtensorMap tm_gu,
                        const __grid_constant__ CUtensorMap tm_down,
+                       const __grid_constant__ CUtensorMap tb_xs,
+                       const __grid_constant__ CUtensorMap tb_attn,
+                       const __grid_constant__ CUtensorMap tb_h,
                        const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -581,6 +559,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tensormap(&tm_o);
     prefetch_tensormap(&tm_gu);
     prefetch_tensormap(&tm_down);
+    prefetch_tensormap(&tb_xs);
+    prefetch_tensormap(&tb_attn);
+    prefetch_tensormap(&tb_h);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 64);
   tc_fence_before();
@@ -592,6 +573,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ---- weight producer: every tile of every GEMM item, in order ----
     if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
       int it = 0;
       for (int l = 0; l < p.n_layers; ++l) {
         for (int gi = 0; gi < N_GEMM; ++gi) {
@@ -600,11 +582,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int mt = w % g.m_tiles, sp = w / g.m_tiles;
             const int kt0 = sp * g.kt_per, kt1 = min(kt0 + g.kt_per, g.k_tiles);
             for (int kt = kt0; kt < kt1; ++kt, ++it) {
-              const int s = it % STAGES;
-              if (!wait_bar(p, &empty[s], ((it / STAGES) & 1) ^ 1)) goto producer_done;
+              const int s = it % p.stages;
+              if (!wait_bar(p, &empty[s], ((it / p.stages) & 1) ^ 1)) goto producer_done;
               mbar_arrive_expect_tx(&full[s], A_BYTES);
-              tma_load_2d(ring + s * A_BYTES, maps[gi], kt * 64,
-                          l * g.rows + mt * 128, &full[s]);
+              tma_load_2d_stream(ring + s * A_BYTES, maps[gi], kt * 64,
+                                 l * g.rows + mt * 128, &full[s], pol);
             }
           }
         }
@@ -627,8 +609,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!wait_bar(p, t_empty, (j & 1) ^ 1)) goto mma_done;
             tc_fence_after();
             for (int kt = kt0; kt < kt1; ++kt, ++it) {
-              const int s = it % STAGES;
-              if (!wait_bar(p, &full[s], (it / STAGES) & 1)) goto mma_done;
+              const int s = it % p.stages;
+              if (!wait_bar(p, &full[s], (it / p.stages) & 1)) goto mma_done;
               tc_fence_after();
               const uint64_t da = smem_desc_sw128(smem_u32(ring + s * A_BYTES));
               const uint64_t db = smem_desc_sw128(bbase + (kt - kt0) * BKT_BYTES);
@@ -648,57 +630,69 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- workers: B builders, epilogues, attention, merges, barriers ----
     const int wtid = threadIdx.x - 64;
     const int q = warp & 3;
+    // epilogue transpose stage: [4 warps][16 tokens][32 features + 4]
+    float* estage = reinterpret_cast<float*>(region + MAX_KT * BKT_BYTES) +
+                    (warp - 2) * 16 * 36;
     const int qkv_ld = (p.heads + 2) * p.hd;
     int j = 0;
+    const bool tr = p.trace && wtid == 0 && cta < 256;
+    if (tr) g_mega_trace[cta][0] = globaltimer_ns();
     for (int l = 0; l < p.n_layers; ++l) {
-      for (int ph = 0; ph < 6; ++ph) {
-        if (ph == 1) {  // attention
+      // phases: 0 prep QKV operand, 1 QKV, 2 finalize q/k/v, 3 attention,
+      // 4 merge, 5 o_proj, 6 prep gate/up operand, 7 gate/up, 8 prep down
+      // operand, 9 down
+      for (int ph = 0; ph < 10; ++ph) {
+        if (ph == 0) {
+          // clear the gate/up accumulators and ss_post (read in ph 8 of the
+          // previous layer), then x*(1+w_in) and ss_in
+          for (int i = cta * 128 + wtid; i < TOK * 2 * p.mlp; i += G * 128)
+            p.acc_gu[i] = 0.f;
+          if (cta == 0 && wtid < TOK) p.ss_post[wtid] = 0.f;
+          prep_scaled(p, p.in_scale + (long long)l * p.width, p.ss_in, wtid);
+        } else if (ph == 2) {
+          finalize_qkv(p, l, wtid);
+        } else if (ph == 3) {
           for (int w = cta; w < p.heads * p.nkb; w += G)
-            attention_item(p, l, w, region, wtid);
-        } else if (ph == 2) {  // merge; clear the QKV accumulators (read in ph 1)
-          for (int r = cta; r < p.heads * p.n_tok; r += G) combine_row(p, r, wtid);
+            attention_item(p, l, w, region, wtid, false);
+        } else if (ph == 4) {  // merge; clear the QKV accumulators (read in ph 2)
+          merge_partials(p, wtid);
+          asm volatile("fence.proxy.async.global;" ::: "memory");
           for (int i = cta * 128 + wtid; i < TOK * qkv_ld; i += G * 128)
             p.acc_qkv[i] = 0.f;
           if (cta == 0 && wtid < TOK) p.ss_in[wtid] = 0.f;
+        } else if (ph == 6) {
+          prep_scaled(p, p.post_scale + (long long)l * p.width, p.ss_post, wtid);
+        } else if (ph == 8) {
+          prep_geglu(p, p.gu_bias ? p.gu_bias + (long long)l * 2 * p.mlp : nullptr, wtid);
         } else {
-          const int gi = ph == 0 ? 0 : ph - 2;  // 0 QKV, 3 O, 4 GU, 5 DOWN
+          const int gi = ph == 1 ? 0 : (ph == 5 ? 1 : (ph == 7 ? 2 : 3));
           const Gemm& g = p.g[gi];
-          if (ph == 0) {  // clear the gate/up accumulators (read in ph 5)
-            for (int i = cta * 128 + wtid; i < TOK * 2 * p.mlp; i += G * 128)
-              p.acc_gu[i] = 0.f;
-            if (cta == 0 && wtid < TOK) p.ss_post[wtid] = 0.f;
-            // ... which must be complete before any item of this phase
-            // starts accumulating ss_in (ss_post is cleared here, ss_in in ph 2)
-          }
+          const CUtensorMap* bmap = gi == 1 ? &tb_attn : (gi == 3 ? &tb_h : &tb_xs);
+          // generic-proxy writes to the region (attention tiles) before the
+          // TMA writes of this phase's B operands
+          fence_async_smem();
+          bar128();
           for (int w = cta; w < g.items; w += G, ++j) {
             const int mt = w % g.m_tiles, sp = w / g.m_tiles;
             const int kt0 = sp * g.kt_per, kt1 = min(kt0 + g.kt_per, g.k_tiles);
             const int nkt = kt1 - kt0;
-            // the previous item's MMAs have finished reading the B region
-            // (its epilogue waited for them); build this item's B
-            if (gi == 0)
-              build_b_scaled(p, region, p.x, p.width, p.in_scale + (long long)l * p.width,
-                             kt0 * 64, nkt, mt == 0 ? p.ss_in : nullptr, wtid);
-            else if (gi == 1)
-              build_b_copy(p, region, p.attn, p.heads * p.hd, kt0 * 64, nkt, wtid);
-            else if (gi == 2)
-              build_b_scaled(p, region, p.x, p.width, p.post_scale + (long long)l * p.width,
-                             kt0 * 64, nkt, mt == 0 ? p.ss_post : nullptr, wtid);
-            else
-              build_b_geglu(p, region, p.gu_bias ? p.gu_bias + (long long)l * 2 * p.mlp : nullptr,
-                            kt0 * 64, nkt, wtid);
-            fence_async_smem();
-            bar128();
-            if (wtid == 0) mbar_arrive(b_full);
+            // B operand (64 tokens x this K slice) by TMA; the previous
+            // item's MMAs have finished reading the region (its epilogue
+            // waited for them)
+            if (wtid == 0) {
+              mbar_arrive_expect_tx(b_full, nkt * BKT_BYTES);
+              for (int i = 0; i < nkt; ++i)
+                tma_load_2d(region + i * BKT_BYTES, bmap, (kt0 + i) * 64, 0, b_full);
+            }
             // epilogue: thread = weight row (output feature), 64 token columns
             const bool ok = wait_bar(p, t_full, j & 1);
             __syncwarp();
             if (ok) {
               tc_fence_after();
-              const int f = mt * 128 + q * 32 + lane;
               float* dst;
               long long ldd;
               float gsc = 1.f;
+              const int f = mt * 128 + q * 32 + lane;  // this thread's row
               if (gi == 0) { dst = p.acc_qkv; ldd = qkv_ld; }
               else if (gi == 2) { dst = p.acc_gu; ldd = 2 * p.mlp; }
               else {
@@ -706,14 +700,32 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const float* gate = gi == 1 ? p.o_gate : p.down_gate;
                 if (gate) gsc = __ldg(gate + (long long)l * p.width + f);
               }
+              // transpose each 16-token chunk through shared memory so that a
+              // lane owns 4 consecutive features of one token: one 16-byte
+              // vector reduction instead of four scalar atomics
+              const int f0 = mt * 128 + q * 32;
 #pragma unroll 1
               for (int c = 0; c < TOK; c += 16) {
+                if (c >= p.n_tok) break;
                 uint32_t r[16];
                 tmem_ld16_sync(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
 #pragma unroll
                 for (int jj = 0; jj < 16; ++jj)
-                  if (c + jj < p.n_tok)
-                    atomicAdd(dst + (long long)(c + jj) * ldd + f, gsc * __uint_as_float(r[jj]));
+                  estage[jj * 36 + lane] = gsc * __uint_as_float(r[jj]);
+                __syncwarp();
+#pragma unroll
+                for (int it = 0; it < 4; ++it) {
+                  const int jj = it * 4 + (lane >> 3);   // token within chunk
+                  const int fq = (lane & 7) * 4;         // 4 features
+                  if (c + jj < p.n_tok) {
+                    const float4 v = *reinterpret_cast<const float4*>(estage + jj * 36 + fq);
+                    float* a = dst + (long long)(c + jj) * ldd + f0 + fq;
+                    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a),
+                                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                                 : "memory");
+                  }
+                }
+                __syncwarp();
               }
             }
             tc_fence_before();
@@ -721,7 +733,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (lane == 0) mbar_arrive(t_empty);
           }
         }
+        if (tr && l == 0) g_mega_trace[cta][1 + 2 * ph] = globaltimer_ns();
         grid_sync(p, wtid);
+        if (tr && l == 0) g_mega_trace[cta][2 + 2 * ph] = globaltimer_ns();
       }
     }
   }

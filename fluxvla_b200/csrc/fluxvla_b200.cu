@@ -169,6 +169,17 @@ int fvb_gemm_trace_next(void) {
   return FVB_OK;
 }
 
+int fvb_expert_trace_read(uint64_t* host_out, int32_t max_ctas) {
+  if (!host_out || max_ctas <= 0)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_expert_trace_read: bad arguments");
+  const int n = max_ctas < 256 ? max_ctas : 256;
+  cudaError_t e = cudaMemcpyFromSymbol(host_out, fvb::mega::g_mega_trace,
+                                       (size_t)n * 32 * sizeof(uint64_t));
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
+  return FVB_OK;
+}
+
 int fvb_gemm_trace_read(uint64_t* host_out, int32_t max_ctas) {
   if (!host_out || max_ctas <= 0)
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm_trace_read: bad arguments");
@@ -490,7 +501,8 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   if (!a) return fail(FVB_ERR_INVALID_ARG, "args is NULL");
   if (a->n_layers <= 0 || a->n_layers > 64 || a->n_tok <= 0 || a->n_tok > TOK ||
       a->width % 128 || a->width <= 0 || a->mlp % 64 || a->mlp <= 0 ||
-      a->head_dim != 256 || a->heads <= 0 || a->n_prefix < 0)
+      a->head_dim != 256 || a->heads <= 0 || a->n_prefix < 0 ||
+      (a->n_prefix + a->n_tok + 63) / 64 > MAX_NKB)
     return fail(FVB_ERR_INVALID_ARG, "fvb_expert_step: unsupported shape");
   Params& p = out->p;
   p.n_layers = a->n_layers; p.n_tok = a->n_tok; p.width = a->width;
@@ -520,8 +532,15 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   p.cache_layer = a->cache_rows * a->head_dim;
   p.key_valid = a->key_valid; p.blocks = a->blocks; p.positions = a->positions;
   p.rope_cs = a->rope_cs;
+  p.rope_suf = a->rope_suffix;
   p.scale_log2 = (1.f / sqrtf((float)a->head_dim)) * 1.4426950408889634f;
   p.nkb = (a->n_prefix + a->n_tok + 63) / 64;
+  p.trace = getenv("FVB_EXPERT_TRACE") ? 1 : 0;
+  p.stages = STAGES;
+  if (getenv("FVB_EXPERT_STAGES")) {
+    const int v = atoi(getenv("FVB_EXPERT_STAGES"));
+    if (v >= 1 && v <= STAGES) p.stages = v;
+  }
   // workspace carve-up (256-byte aligned pieces)
   char* base = (char*)a->workspace;
   long long off = 0;
@@ -537,7 +556,11 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   p.part_o = (float*)take((long long)a->heads * p.nkb * TOK * a->head_dim * 4);
   p.part_ml = (float*)take((long long)a->heads * p.nkb * TOK * 2 * 4);
   p.attn = (bf16*)take((long long)TOK * a->heads * a->head_dim * 2);
-  p.bar = (unsigned*)take(64);
+  p.qb = (bf16*)take((long long)TOK * a->heads * a->head_dim * 2);
+  p.xs = (bf16*)take((long long)TOK * a->width * 2);
+  p.hb = (bf16*)take((long long)TOK * a->mlp * 2);
+  p.kvs = (bf16*)take((long long)2 * 128 * a->head_dim * 2);
+  p.bar = (unsigned*)take(BAR_WORDS * 4);
   out->bytes = off;
   return FVB_OK;
 }
@@ -559,7 +582,7 @@ extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
   if (r) return r;
   if (!a->w_qkv || !a->w_o || !a->w_gu || !a->w_down || !a->in_scale ||
       !a->post_scale || !a->x || !a->k_cache || !a->v_cache || !a->blocks ||
-      !a->positions || !a->rope_cs)
+      !a->positions || !a->rope_cs || !a->rope_suffix)
     return fail(FVB_ERR_INVALID_ARG, "fvb_expert_step: NULL operand");
   if (!a->workspace || a->workspace_bytes < L.bytes || !aligned16(a->workspace))
     return fail(FVB_ERR_WORKSPACE, "fvb_expert_step: workspace needs %lld bytes",
@@ -572,6 +595,12 @@ extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
                  (long long)p.g[i].k_tiles * 64, (long long)p.g[i].k_tiles * 64, 128);
     if (r) return r;
   }
+  CUtensorMap bmaps[3];
+  r = make_map(&bmaps[0], p.xs, TOK, a->width, a->width, TOK);
+  if (!r) r = make_map(&bmaps[1], p.attn, TOK, (long long)a->heads * a->head_dim,
+                       (long long)a->heads * a->head_dim, TOK);
+  if (!r) r = make_map(&bmaps[2], p.hb, TOK, a->mlp, a->mlp, TOK);
+  if (r) return r;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(expert_step_kernel,
@@ -592,7 +621,8 @@ extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, expert_step_kernel, maps[0], maps[1],
-                                     maps[2], maps[3], p);
+                                     maps[2], maps[3], bmaps[0], bmaps[1],
+                                     bmaps[2], p);
   if (e != cudaSuccess)
     return fail(FVB_ERR_CUDA, "fvb_expert_step: launch failed: %s",
                 cudaGetErrorString(e));

@@ -220,6 +220,7 @@ class PI0EngineB200:
         B['gemm_ws'] = z(ws, dt=torch.uint8)
         max_pos = E + S + 8
         B['rope'] = rope_table(max_pos, hd, device=d)
+        B['rope_suffix'] = z(S, hd // 2, 2, dt=F32)
         self.B = B
         self.mean3 = list(cfg.img_mean)
         self.std3 = list(cfg.img_std)
@@ -308,7 +309,8 @@ class PI0EngineB200:
                  w_gu=P['exp.gu_all'], w_down=P['exp.down_w_all'],
                  x=B['e_res'], k_cache=B['kc'], v_cache=B['vc'],
                  key_valid=B['key_valid'], blocks=B['blocks'],
-                 positions=B['pos_suffix'], rope_cs=B['rope'])
+                 positions=B['pos_suffix'], rope_cs=B['rope'],
+                 rope_suffix=B['rope_suffix'])
         a.update(self.step_tables[k])
         if 'expert_ws' not in B:
             nbytes = ops.expert_workspace_bytes(ops.expert_args(**a))
@@ -509,8 +511,11 @@ class PI0EngineB200:
         pos = (torch.cumsum(kv, 0) - 1).clamp(min=0).to(torch.int32)
         self.B['key_valid'].copy_(kv.to(torch.uint8))
         self.B['pos_prefix'].copy_(pos)
-        self.B['pos_suffix'].copy_(
-            (int(kv.sum()) + torch.arange(self.S)).to(torch.int32))
+        pos_suf = (int(kv.sum()) + torch.arange(self.S)).to(torch.int32)
+        self.B['pos_suffix'].copy_(pos_suf)
+        # rotary cos/sin of the suffix positions, gathered once per request
+        self.B['rope_suffix'].copy_(
+            self.B['rope'][pos_suf.to(self.B['rope'].device).long()])
 
     def load_inputs(self, images_u8=None, lang_tokens=None, lang_masks=None,
                     img_masks=None, state=None, noise=None):

@@ -170,7 +170,7 @@ def launch_count() -> int:
 
 def expert_args(*, n_layers, n_tok, width, mlp, heads, head_dim, n_prefix,
                 w_qkv, w_o, w_gu, w_down, in_scale, post_scale, x, k_cache,
-                v_cache, blocks, positions, rope_cs, qkv_bias=None,
+                v_cache, blocks, positions, rope_cs, rope_suffix=None, qkv_bias=None,
                 gu_bias=None, o_gate=None, down_gate=None, key_valid=None,
                 eps=1e-6, workspace=None) -> ExpertArgs:
     return ExpertArgs(
@@ -183,7 +183,8 @@ def expert_args(*, n_layers, n_tok, width, mlp, heads, head_dim, n_prefix,
         k_cache=_ptr(k_cache), v_cache=_ptr(v_cache),
         cache_rows=k_cache.shape[1], key_valid=_ptr(key_valid),
         blocks=_ptr(blocks), positions=_ptr(positions),
-        rope_cs=_ptr(rope_cs), workspace=_ptr(workspace),
+        rope_cs=_ptr(rope_cs), rope_suffix=_ptr(rope_suffix),
+        workspace=_ptr(workspace),
         workspace_bytes=0 if workspace is None else
         workspace.numel() * workspace.element_size())
 

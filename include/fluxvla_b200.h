@@ -201,6 +201,8 @@ typedef struct fvb_expert_args {
                               * iff blocks[s] <= blocks[t]                  */
   const int32_t* positions;  /* [n_tok] RoPE positions                      */
   const float* rope_cs;      /* [max_pos, head_dim/2, 2]                    */
+  const float* rope_suffix;  /* [n_tok, head_dim/2, 2]: rope_cs rows at
+                              * positions[t] (gathered once per request)     */
   void* workspace;           /* fvb_expert_workspace_bytes(); zero-filled
                               * before the first call, left reusable        */
   int64_t workspace_bytes;
@@ -264,6 +266,10 @@ int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
  * CTAs; fvb_gemm_trace_read copies them (8 x uint64 per CTA) to the host. */
 int fvb_gemm_trace_next(void);
 int fvb_gemm_trace_read(uint64_t* host_out, int32_t max_ctas);
+/* Diagnostics: with FVB_EXPERT_TRACE set in the environment,
+ * fvb_expert_step records per CTA (32 x uint64 each) the worker start and,
+ * for layer 0, the end of each phase's work and of its grid barrier. */
+int fvb_expert_trace_read(uint64_t* host_out, int32_t max_ctas);
 
 /* Status and diagnostics. */
 int fvb_get_device_status(int* status, int reset);
