@@ -157,9 +157,16 @@ __device__ __forceinline__ void warp_writeback(
     if (row >= rows_valid) continue;
     uint32_t* d = dst_of_row(row) + w0 + extra;
     if (MODE == 2) {
+      if (vec) {
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(d),
+                     "f"(val[it][0]), "f"(val[it][1]), "f"(val[it][2]),
+                     "f"(val[it][3])
+                     : "memory");
+      } else {
 #pragma unroll
-      for (int w = 0; w < 4; ++w)
-        if (w0 + w < words_valid) atomicAdd(reinterpret_cast<float*>(d) + w, val[it][w]);
+        for (int w = 0; w < 4; ++w)
+          if (w0 + w < words_valid) atomicAdd(reinterpret_cast<float*>(d) + w, val[it][w]);
+      }
     } else if (vec) {
       *reinterpret_cast<uint4*>(d) =
           make_uint4(__float_as_uint(val[it][0]), __float_as_uint(val[it][1]),

@@ -345,16 +345,17 @@ class PI0EngineB200:
             p = f'vision.l{i}.'
             ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P[p + 'ln1_w'],
                      b=P[p + 'ln1_b'])
-            ops.gemm(B['v_xn'], P[p + 'qkv_w'], qkv, bias=P[p + 'qkv_b'])
+            ops.gemm(B['v_xn'], P[p + 'qkv_w'], qkv, bias=P[p + 'qkv_b'],
+                     block_n=256)
             ops.attention(attn)
             ops.gemm(B['v_ao'], P[p + 'o_w'], B['v_res'], epilogue=EPI_F32_ACC,
                      bias=P[p + 'o_b'], split_k=2)
             ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P[p + 'ln2_w'],
                      b=P[p + 'ln2_b'])
             ops.gemm(B['v_xn'], P[p + 'fc1_w'], B['v_h'], bias=P[p + 'fc1_b'],
-                     act=ACT_GELU_TANH)
+                     act=ACT_GELU_TANH, block_n=256)
             ops.gemm(B['v_h'], P[p + 'fc2_w'], B['v_res'], epilogue=EPI_F32_ACC,
-                     bias=P[p + 'fc2_b'], split_k=3)
+                     bias=P[p + 'fc2_b'], split_k=2)
         ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P['post_w'],
                  b=P['post_b'])
         ops.gemm(B['v_xn'], P['proj_w'], B['l_res'][:R], epilogue=EPI_F32_STORE,
@@ -381,13 +382,14 @@ class PI0EngineB200:
                 q_head_stride=hd, k_row_stride=hd, k_head_stride=0,
                 v_row_stride=hd, v_head_stride=0, o_row_stride=H * hd,
                 o_head_stride=hd, key_valid=B['key_valid'], n_prefix=E))
-            ops.gemm(B['l_ao'], P[p + 'o_w'], B['l_res'], epilogue=EPI_F32_ACC)
+            ops.gemm(B['l_ao'], P[p + 'o_w'], B['l_res'], epilogue=EPI_F32_ACC,
+                     block_n=256, split_k=2)
             ops.norm(NORM_GEMMA_RMS, B['l_res'], B['l_xn'],
                      w=P[p + 'post_norm'])
             ops.gemm(B['l_xn'], P[p + 'gu'], B['l_h'], epilogue=EPI_GEGLU,
                      block_n=256)
             ops.gemm(B['l_h'], P[p + 'down_w'], B['l_res'],
-                     epilogue=EPI_F32_ACC, split_k=2)
+                     epilogue=EPI_F32_ACC, block_n=256, split_k=5)
 
     def _state_token(self):
         if self.cfg.has_state_token:
