@@ -329,38 +329,53 @@ def run_b200(args):
     barrier()
     assert torch.isfinite(out).all()
 
-    # ---- roofline: dominant kernel timed alone with CUDA events ----
+    # ---- roofline: the dominant kernel (the persistent expert step, one
+    # launch per denoise step) timed alone with CUDA events on its stream;
+    # algorithmic bytes per launch = expert weights + prefix K/V of all layers
     peaks, peak_kind = load_peaks()
+    L = cfg.exp_layers
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    xargs = eng._expert_args(0)
+    saved = eng.B['e_res'].clone()
+    reps = 20
+    ev[0].record(stream)
+    for _ in range(reps):
+        ops.expert_step(xargs)
+    ev[1].record(stream)
+    torch.cuda.synchronize(dev)
+    eng.B['e_res'].copy_(saved)
+    t_launch = ev[0].elapsed_time(ev[1]) / reps * 1e-3
+    wbytes = sum(eng.P[f'exp.{n}_all'].numel() * 2
+                 for n in ('qkv', 'o_w', 'gu', 'down_w'))
+    kvbytes = 2 * L * E * cfg.head_dim * 2
+    ach = (wbytes + kvbytes) / t_launch / 1e9
+    roof = {'kernel': f'fvb::mega::expert_step_kernel ({L} expert layers of one '
+                      'denoise step, persistent, 148 CTAs)',
+            'bound': 'hbm', 'achieved': ach, 'peak': peaks['hbm_gbs'],
+            'unit': 'GB/s', 'frac': ach / peaks['hbm_gbs'],
+            'peak_source': f'{peak_kind} HBM copy (kernel timed alone)',
+            'traffic': None, 'launch_us': t_launch * 1e6,
+            'algorithmic_bytes_per_launch': wbytes + kvbytes}
+    roof_prefill = None
     if w != 'loop':
         P, B = eng.P, eng.B
-        reps, L = 3, cfg.llm_layers - 1
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        reps, Lp = 3, cfg.llm_layers - 1
         ev[0].record(stream)
         for _ in range(reps):
-            for i in range(L):
+            for i in range(Lp):
                 ops.gemm(B['l_xn'], P[f'llm.l{i}.gu'], B['l_h'],
                          epilogue=EPI_GEGLU, block_n=256)
         ev[1].record(stream)
         torch.cuda.synchronize(dev)
-        t_launch = ev[0].elapsed_time(ev[1]) / (reps * L) * 1e-3
+        t_g = ev[0].elapsed_time(ev[1]) / (reps * Lp) * 1e-3
         flops = 2.0 * E * cfg.llm_width * 2 * cfg.llm_mlp
-        ach = flops / t_launch / 1e12
-        roof = {'kernel': 'gemm_tc_kernel<256,4> Gemma-2B gate/up GeGLU '
-                          f'[{E}x2048]x[32768x2048]^T',
-                'bound': 'tensor', 'achieved': ach,
-                'peak': peaks['bf16_tflops'], 'unit': 'TFLOP/s',
-                'frac': ach / peaks['bf16_tflops'],
-                'peak_source': f'{peak_kind} burst bf16 (kernel timed alone)',
-                'traffic': None, 'launch_us': t_launch * 1e6}
-    else:
-        wbytes = sum(v.numel() * v.element_size() for k, v in eng.P.items()
-                     if k.startswith('exp.'))
-        kvb = 2 * cfg.exp_layers * E * cfg.head_dim * 2
-        ach = (wbytes + kvb) * len(eng.times) / (ms * 1e-3) / 1e9
-        roof = {'kernel': 'denoise chunk (all loop kernels)', 'bound': 'hbm',
-                'achieved': ach, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
-                'frac': ach / peaks['hbm_gbs'],
-                'peak_source': f'{peak_kind} HBM copy', 'traffic': None}
+        roof_prefill = {
+            'kernel': 'gemm_tc_kernel<256,4,GEGLU> Gemma-2B gate/up '
+                      f'[{E}x2048]x[32768x2048]^T', 'bound': 'tensor',
+            'achieved': flops / t_g / 1e12, 'peak': peaks['bf16_tflops'],
+            'unit': 'TFLOP/s', 'frac': flops / t_g / 1e12 / peaks['bf16_tflops'],
+            'peak_source': f'{peak_kind} burst bf16 (kernel timed alone)',
+            'launch_us': t_g * 1e6}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -391,7 +406,8 @@ def run_b200(args):
             'e2e': {'value': world * 1000.0 / e2e_ms, 'unit': 'chunks/s',
                     'latency_ms': e2e_ms, 'h2d_bytes_per_step': int(h2d),
                     'd2h_bytes_per_step': int(d2h)},
-            'roofline': roof, 'cpu_baseline': cpu,
+            'roofline': roof, 'roofline_prefill_gemm': roof_prefill,
+            'cpu_baseline': cpu,
             'gpu_launches': int(eng.launches_per_call * args.steps),
             'launches_per_chunk': eng.launches_per_call,
             'clocks': clocks,
