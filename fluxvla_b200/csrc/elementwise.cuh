@@ -79,6 +79,65 @@ __global__ void __launch_bounds__(NORM_THREADS)
   }
 }
 
+// Same norms with one warp per row (8 rows per CTA) for dim % 128 == 0 and
+// dim <= 2048: each lane holds its dim/32 values in registers, so the row is
+// read once and reduced with shuffles only.
+constexpr int NORM_ROWS_PER_CTA = 8;
+template <int V4>  // float4 per lane = dim / 128
+__global__ void __launch_bounds__(256)
+    norm_warp_kernel(int mode, const float* __restrict__ x, long long ld_in,
+                     void* __restrict__ out, long long ld_out, int out_f32,
+                     int rows, int dim, const bf16* __restrict__ w,
+                     const bf16* __restrict__ b, const float* __restrict__ mod,
+                     float eps) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * NORM_ROWS_PER_CTA + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + (long long)row * ld_in;
+  float4 v[V4];
+  float s = 0.f, ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    v[i] = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
+    s += v[i].x + v[i].y + v[i].z + v[i].w;
+    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  float mean = 0.f, rstd;
+  if (mode == FVB_NORM_LAYER) {
+    mean = warp_sum(s) / dim;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V4; ++i)
+      q += (v[i].x - mean) * (v[i].x - mean) + (v[i].y - mean) * (v[i].y - mean) +
+           (v[i].z - mean) * (v[i].z - mean) + (v[i].w - mean) * (v[i].w - mean);
+    rstd = rsqrtf(warp_sum(q) / dim + eps);
+  } else {
+    rstd = rsqrtf(warp_sum(ss) / dim + eps);
+  }
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    const int c0 = (i * 32 + lane) * 4;
+    float y[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = c0 + e;
+      float t = (y[e] - mean) * rstd;
+      if (mode == FVB_NORM_GEMMA_RMS) t *= 1.f + __bfloat162float(w[c]);
+      else if (mode == FVB_NORM_ADA_RMS) t = t * (1.f + mod[c]) + mod[dim + c];
+      else t = t * __bfloat162float(w[c]) + __bfloat162float(b[c]);
+      y[e] = t;
+    }
+    if (out_f32)
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (long long)row * ld_out + c0) =
+          make_float4(y[0], y[1], y[2], y[3]);
+    else
+      *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(out) + (long long)row * ld_out + c0) =
+          make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+  }
+}
+
 // uint8 HWC images -> normalised bf16 patch rows.  One CTA per patch row.
 __global__ void patchify_kernel(const uint8_t* __restrict__ img, int H, int W,
                                 int P, float m0, float m1, float m2, float s0,

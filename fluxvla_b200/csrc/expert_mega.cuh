@@ -645,8 +645,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (ph == 0) {
           // clear the gate/up accumulators and ss_post (read in ph 8 of the
           // previous layer), then x*(1+w_in) and ss_in
-          for (int i = cta * 128 + wtid; i < TOK * 2 * p.mlp; i += G * 128)
-            p.acc_gu[i] = 0.f;
+          for (int i = cta * 128 + wtid; i < p.n_tok * 2 * p.mlp / 4; i += G * 128)
+            reinterpret_cast<float4*>(p.acc_gu)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
           if (cta == 0 && wtid < TOK) p.ss_post[wtid] = 0.f;
           prep_scaled(p, p.in_scale + (long long)l * p.width, p.ss_in, wtid);
         } else if (ph == 2) {
@@ -657,8 +657,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (ph == 4) {  // merge; clear the QKV accumulators (read in ph 2)
           merge_partials(p, wtid);
           asm volatile("fence.proxy.async.global;" ::: "memory");
-          for (int i = cta * 128 + wtid; i < TOK * qkv_ld; i += G * 128)
-            p.acc_qkv[i] = 0.f;
+          for (int i = cta * 128 + wtid; i < p.n_tok * qkv_ld / 4; i += G * 128)
+            reinterpret_cast<float4*>(p.acc_qkv)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
           if (cta == 0 && wtid < TOK) p.ss_in[wtid] = 0.f;
         } else if (ph == 6) {
           prep_scaled(p, p.post_scale + (long long)l * p.width, p.ss_post, wtid);
@@ -680,9 +680,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             // item's MMAs have finished reading the region (its epilogue
             // waited for them)
             if (wtid == 0) {
+              // the m_tiles CTAs of one K slice read the same B tiles; start
+              // each at a different k-tile so their requests spread over L2
               mbar_arrive_expect_tx(b_full, nkt * BKT_BYTES);
-              for (int i = 0; i < nkt; ++i)
+              for (int i0 = 0; i0 < nkt; ++i0) {
+                const int i = (i0 + mt) % nkt;
                 tma_load_2d(region + i * BKT_BYTES, bmap, (kt0 + i) * 64, 0, b_full);
+              }
             }
             // epilogue: thread = weight row (output feature), 64 token columns
             const bool ok = wait_bar(p, t_full, j & 1);

@@ -436,6 +436,25 @@ int fvb_norm(int32_t mode, const float* x, int64_t ld_in, void* out,
     return fail(FVB_ERR_INVALID_ARG, "fvb_norm: weight and bias required");
   if (mode < 0 || mode > 2)
     return fail(FVB_ERR_INVALID_ARG, "fvb_norm: bad mode");
+  if (dim % 128 == 0 && dim <= 2048 && rows >= 64) {
+    const dim3 grid((rows + fvb::NORM_ROWS_PER_CTA - 1) / fvb::NORM_ROWS_PER_CTA);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define FVB_NORM_WARP(V)                                                      \
+  return launch_k("fvb_norm", fvb::norm_warp_kernel<V>, grid, dim3(256), 0,   \
+                  st, (int)mode, x, (long long)ld_in, out, (long long)ld_out, \
+                  (int)out_f32, (int)rows, (int)dim, (const bf16*)w,          \
+                  (const bf16*)b, mod, eps);
+    switch (dim / 128) {
+      case 1: FVB_NORM_WARP(1)
+      case 2: FVB_NORM_WARP(2)
+      case 4: FVB_NORM_WARP(4)
+      case 8: FVB_NORM_WARP(8)
+      case 9: FVB_NORM_WARP(9)
+      case 16: FVB_NORM_WARP(16)
+      default: break;
+    }
+#undef FVB_NORM_WARP
+  }
   return launch_k("fvb_norm", fvb::norm_kernel, dim3(rows),
                   dim3(fvb::NORM_THREADS), 0,
                   reinterpret_cast<cudaStream_t>(stream), (int)mode, x,

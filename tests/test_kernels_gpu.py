@@ -246,9 +246,9 @@ def test_attention_siglip_hd72_views():
 
 @pytest.mark.parametrize('mode', [NORM_GEMMA_RMS, NORM_ADA_RMS, NORM_LAYER])
 @pytest.mark.parametrize('out_f32', [False, True])
-def test_norm(mode, out_f32):
+@pytest.mark.parametrize('R,D', [(51, 1024), (816, 2048), (768, 1152), (70, 1000)])
+def test_norm(mode, out_f32, R, D):
     torch.manual_seed(10)
-    R, D = 51, 1024
     x = torch.randn(R, D, device=DEV) * 3 + 0.5
     w = rnd(D, std=0.02) + (1 if mode == NORM_LAYER else 0)
     b = rnd(D, std=0.02)
