@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "common.cuh"
 #include "elementwise.cuh"
 #include "expert_mega.cuh"
@@ -76,6 +77,42 @@ int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t k,
   return FVB_OK;
 }
 
+// Output tensor map of a normal-orientation GEMM epilogue: [rows, cols] of
+// f32 or bf16 (row stride ld elements), box [32, box_cols] with the swizzle
+// whose span equals the box row (64 or 32 bytes).
+int make_out_map(CUtensorMap* m, void* ptr, bool f32, int64_t rows,
+                 int64_t cols, int64_t ld, int box_cols) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return fail(FVB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int eb = f32 ? 4 : 2;
+  const int row_bytes = box_cols * eb;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * eb)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   2, ptr, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FVB_ERR_INVALID_ARG, "output tensor map encode failed (%d)", (int)r);
+  return FVB_OK;
+}
+
+// TMA-store epilogues are on unless FVB_TMA_OUT=0.
+bool tma_out_enabled() {
+  static const int v = [] {
+    const char* e = getenv("FVB_TMA_OUT");
+    return e ? atoi(e) : 1;
+  }();
+  return v != 0;
+}
+
 // Programmatic dependent launch is on unless FVB_PDL=0: each kernel may
 // start its prologue (and the GEMMs their weight prefetch) while the
 // previous kernel in the stream drains; every kernel executes
@@ -122,7 +159,7 @@ int sm_count() {
 
 template <int BN, int EPI, bool SWAP, int ACT = FVB_ACT_NONE>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
-                const fvb::GemmDev& d, cudaStream_t st) {
+                const CUtensorMap& mo, const fvb::GemmDev& d, cudaStream_t st) {
   using C = fvb::GemmCfg<BN>;
   auto kern = fvb::gemm_tc_kernel<BN, C::STAGES, EPI, SWAP, ACT>;
   static bool attr = false;
@@ -135,7 +172,54 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
   }
   const int grid = d.n_work < sm_count() ? d.n_work : sm_count();
   return launch_k("fvb_gemm", kern, dim3(grid), dim3(fvb::GEMM_THREADS),
-                  (size_t)C::SMEM, st, ma, mb, d);
+                  (size_t)C::SMEM, st, ma, mb, mo, d);
+}
+
+// Tensor-core attention for unsplit attention without suffix block masks
+// (the SigLIP and Gemma prefix prefills); on unless FVB_ATTN_TC=0.
+bool attn_tc_enabled() {
+  static const int v = [] {
+    const char* e = getenv("FVB_ATTN_TC");
+    return e ? atoi(e) : 1;
+  }();
+  return v != 0;
+}
+
+template <int HD, int HDP, int NV>
+int launch_attn_tc(const fvb_attn_args* a, const fvb::AttnDev& d,
+                          cudaStream_t st) {
+  namespace A = fvb::atc;
+  using C = A::AtcCfg<HD, HDP, NV>;
+  const long long kv_rows = (long long)(a->batch - 1) * a->kv_batch_rows + a->n_kv;
+  // the maps span exactly the K / V heads' columns of each row, so a box
+  // reaching past the last head reads zeros instead of memory beyond the view
+  const int kv_heads = a->heads / a->group;
+  const long long k_cols = (long long)(kv_heads - 1) * a->k_head_stride + a->head_dim;
+  const long long v_cols = (long long)(kv_heads - 1) * a->v_head_stride + a->head_dim;
+  CUtensorMap mk, mv;
+  int r = make_map(&mk, a->k, kv_rows, k_cols, a->k_row_stride, A::BKV);
+  if (!r) r = make_map(&mv, a->v, kv_rows, v_cols, a->v_row_stride, A::BKV);
+  if (r) return r;
+  A::AtcDev p;
+  p.q = d.q; p.q_rs = d.q_rs; p.q_hs = d.q_hs;
+  p.o = d.o; p.o_rs = d.o_rs; p.o_hs = d.o_hs;
+  p.k_hs = (int)a->k_head_stride; p.v_hs = (int)a->v_head_stride;
+  p.n_q = a->n_q; p.n_kv = a->n_kv; p.group = a->group;
+  p.q_br = a->q_batch_rows; p.kv_br = a->kv_batch_rows;
+  p.scale_log2 = d.scale_log2;
+  p.key_valid = a->key_valid;
+  auto kern = A::attn_tc_kernel<HD, HDP, NV>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM) != cudaSuccess)
+      return fail(FVB_ERR_CUDA, "attention smem attribute: %s",
+                  cudaGetErrorString(cudaGetLastError()));
+    attr = true;
+  }
+  const int tiles = (a->group * a->n_q + A::BM - 1) / A::BM;
+  return launch_k("fvb_attention", kern, dim3(tiles, a->heads / a->group, a->batch),
+                  dim3(A::THREADS), (size_t)C::SMEM, st, mk, mv, p);
 }
 
 int g_trace_next = 0;
@@ -297,6 +381,25 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   d.trace = g_trace_next ? 1 : 0;
   g_trace_next = 0;
 
+  // TMA-store epilogue: normal orientation, plain row-major output rows on
+  // 16-byte boundaries (the position-embedding add and QKV+RoPE keep the
+  // per-row write-back)
+  CUtensorMap mo;
+  memset(&mo, 0, sizeof(mo));
+  d.tma_out = 0;
+  if (!a->swap && tma_out_enabled() && aligned16(a->out)) {
+    const int e = a->epilogue;
+    const bool f32 = e == FVB_EPI_F32_ACC || (e == FVB_EPI_F32_STORE && !a->row_add);
+    const bool b16 = e == FVB_EPI_BF16 || e == FVB_EPI_GEGLU;
+    if ((f32 && a->ldo % 4 == 0) || (b16 && a->ldo % 8 == 0)) {
+      const int64_t cols = e == FVB_EPI_GEGLU ? a->n / 2 : a->n;
+      const int box_cols = (f32 || e == FVB_EPI_GEGLU) ? 16 : 32;
+      r = make_out_map(&mo, a->out, f32, a->m, cols, a->ldo, box_cols);
+      if (r) return r;
+      d.tma_out = 1;
+    }
+  }
+
   d.m_tiles = (a->m + fvb::GEMM_BM - 1) / fvb::GEMM_BM;
   d.n_tiles = (a->n + bn - 1) / bn;
   d.n_work = d.m_tiles * d.n_tiles * d.split;
@@ -305,14 +408,14 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   switch (a->epilogue) {                                                   \
     case FVB_EPI_BF16:                                                     \
       if (a->act == FVB_ACT_GELU_TANH)                                     \
-        return launch_gemm<BN, FVB_EPI_BF16, SWAP, FVB_ACT_GELU_TANH>(ma, mb, d, st); \
+        return launch_gemm<BN, FVB_EPI_BF16, SWAP, FVB_ACT_GELU_TANH>(ma, mb, mo, d, st); \
       if (a->act == FVB_ACT_SILU)                                          \
-        return launch_gemm<BN, FVB_EPI_BF16, SWAP, FVB_ACT_SILU>(ma, mb, d, st); \
-      return launch_gemm<BN, FVB_EPI_BF16, SWAP>(ma, mb, d, st);           \
-    case FVB_EPI_F32_STORE: return launch_gemm<BN, FVB_EPI_F32_STORE, SWAP>(ma, mb, d, st); \
-    case FVB_EPI_F32_ACC: return launch_gemm<BN, FVB_EPI_F32_ACC, SWAP>(ma, mb, d, st); \
-    case FVB_EPI_GEGLU: return launch_gemm<BN, FVB_EPI_GEGLU, SWAP>(ma, mb, d, st); \
-    default: return launch_gemm<BN, FVB_EPI_QKV_ROPE, SWAP>(ma, mb, d, st); \
+        return launch_gemm<BN, FVB_EPI_BF16, SWAP, FVB_ACT_SILU>(ma, mb, mo, d, st); \
+      return launch_gemm<BN, FVB_EPI_BF16, SWAP>(ma, mb, mo, d, st);           \
+    case FVB_EPI_F32_STORE: return launch_gemm<BN, FVB_EPI_F32_STORE, SWAP>(ma, mb, mo, d, st); \
+    case FVB_EPI_F32_ACC: return launch_gemm<BN, FVB_EPI_F32_ACC, SWAP>(ma, mb, mo, d, st); \
+    case FVB_EPI_GEGLU: return launch_gemm<BN, FVB_EPI_GEGLU, SWAP>(ma, mb, mo, d, st); \
+    default: return launch_gemm<BN, FVB_EPI_QKV_ROPE, SWAP>(ma, mb, mo, d, st); \
   }
   if (a->swap) FVB_EPI_CASES(64, true)
   if (bn == 64) FVB_EPI_CASES(64, false)
@@ -381,6 +484,11 @@ int fvb_attention(const fvb_attn_args* a, void* stream) {
                   need);
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (d.splits == 1 && a->n_prefix >= a->n_kv && attn_tc_enabled() &&
+      aligned16(a->o) && a->o_row_stride % 8 == 0 && a->o_head_stride % 8 == 0) {
+    if (a->head_dim == 256) return launch_attn_tc<256, 256, 256>(a, d, st);
+    return launch_attn_tc<72, 128, 80>(a, d, st);
+  }
   dim3 grid((a->n_q + fvb::ATT_BM - 1) / fvb::ATT_BM, a->heads,
             a->batch * d.splits);
   if (a->head_dim == 256) {

@@ -58,6 +58,8 @@ struct GemmDev {
   float* ws;
   unsigned* ws_cnt;
   int trace;  // diagnostics: record per-CTA phase times in g_gemm_trace
+  int tma_out;  // normal orientation: the epilogue writes through the output
+                // tensor map (TMA store, or TMA f32 reduce-add for F32_ACC)
 };
 
 __device__ __forceinline__ void epi_bar_sync() {
@@ -440,6 +442,111 @@ __device__ __forceinline__ void epilogue_normal(const GemmDev& p, const EpiPre& 
 }
 
 // ---------------------------------------------------------------------------
+// Normal orientation epilogue through TMA: per group of 32 accumulator
+// columns the warp converts its 32 rows into swizzled 32-row boxes in its
+// shared-memory buffer and one lane issues an asynchronous TMA store (BF16,
+// F32_STORE, GEGLU) or TMA f32 reduce-add (F32_ACC: out += y, which also
+// merges K splits in L2).  The warp's 4 KB buffer holds two 2 KB box slots,
+// so a box is written while the previous one is still being read by the
+// TMA unit, and the TMEM read of the next group is issued before the
+// current group is converted: TMEM latency, conversion and stores overlap.
+// Boxes (32 rows each): f32 16 columns (64 B rows), bf16 32 columns (64 B
+// rows), GEGLU 16 bf16 columns (32 B rows); the swizzle span equals the row
+// size.  Swizzle of byte offset o inside a slot: the 16-byte chunk bits
+// [4, 4+b) are XORed with bits [7, 7+b), b = log2(row bytes / 16).
+// ---------------------------------------------------------------------------
+template <int EPI>
+struct TmaBox {
+  static constexpr bool F32 = EPI == FVB_EPI_F32_STORE || EPI == FVB_EPI_F32_ACC;
+  static constexpr int ROW_BYTES = EPI == FVB_EPI_GEGLU ? 32 : 64;
+  static constexpr int COLS = F32 ? 16 : (EPI == FVB_EPI_GEGLU ? 16 : 32);
+  static constexpr int PER_GROUP = F32 ? 2 : 1;  // boxes per 32 accumulator columns
+  static constexpr uint32_t SW = ROW_BYTES == 64 ? 3u : 1u;
+  static constexpr uint32_t SLOT = 2048;
+};
+
+template <int BN, int EPI, int ACT>
+__device__ __forceinline__ void epilogue_tma(const GemmDev& p,
+                                             const CUtensorMap* tmO,
+                                             const float* colv, uint32_t taddr,
+                                             uint8_t* buf, int t_base,
+                                             int bcol0, int lane) {
+  using BX = TmaBox<EPI>;
+  constexpr int RB = BX::ROW_BYTES;
+  constexpr int NCH = RB / 16;   // 16-byte chunks per box row
+  constexpr int WPB = RB / 4;    // 32-bit words per box row
+  if (t_base >= p.m) return;  // whole warp past the last token row
+  const int ng = min(BN / 32, (p.n - bcol0 + 31) / 32);
+  const uint32_t sbuf = smem_u32(buf);
+  const uint32_t o_row = (uint32_t)(lane * RB);
+  uint32_t slot = 0;
+  uint32_t cur[32], nxt[32];
+  tmem_ld32(taddr, cur);
+  tmem_wait_ld32(cur);
+  __syncwarp();  // column vectors visible
+  const bool tr = p.trace && lane == 0 && (t_base & 127) == 64;
+  if (tr) trace_stamp(p, 8);
+#pragma unroll 1
+  for (int g = 0; g < ng; ++g) {
+    const int c = g * 32;
+    if (g + 1 < ng) tmem_ld32(taddr + (uint32_t)(c + 32), nxt);
+    uint32_t w[32];
+    if (EPI == FVB_EPI_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 2)
+        w[j >> 1] = pack_bf16x2(
+            apply_act<ACT>(p.alpha * u2f(cur[j]) + colv[c + j]),
+            apply_act<ACT>(p.alpha * u2f(cur[j + 1]) + colv[c + j + 1]));
+    } else if (EPI == FVB_EPI_GEGLU) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 2)
+        w[i >> 1] = pack_bf16x2(gelu_tanh_f(u2f(cur[2 * i])) * u2f(cur[2 * i + 1]),
+                                gelu_tanh_f(u2f(cur[2 * i + 2])) * u2f(cur[2 * i + 3]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float y = u2f(cur[j]) + colv[c + j];
+        if (EPI == FVB_EPI_F32_ACC) y *= colv[BN + c + j];
+        w[j] = __float_as_uint(y);
+      }
+    }
+#pragma unroll
+    for (int bx = 0; bx < BX::PER_GROUP; ++bx) {
+      if (lane == 0) bulk_wait_read1();  // this slot's previous box was read
+      __syncwarp();
+      const uint32_t sb = sbuf + slot * BX::SLOT;
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const uint32_t o = o_row + (uint32_t)(ch * 16);
+        const uint32_t phys = o ^ (((o >> 7) & BX::SW) << 4);
+        const int w0 = bx * WPB + 4 * ch;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sb + phys),
+                     "r"(w[w0]), "r"(w[w0 + 1]), "r"(w[w0 + 2]), "r"(w[w0 + 3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int col = bcol0 + c + bx * BX::COLS;
+        const int x = EPI == FVB_EPI_GEGLU ? col >> 1 : col;
+        if (EPI == FVB_EPI_F32_ACC)
+          tma_reduce_add_2d(tmO, x, t_base, buf + slot * BX::SLOT);
+        else
+          tma_store_2d(tmO, x, t_base, buf + slot * BX::SLOT);
+        bulk_commit();
+      }
+      slot ^= 1u;
+    }
+    if (tr && g < 2) trace_stamp(p, 9 + g);
+    if (g + 1 < ng) {
+      tmem_wait_ld32(nxt);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Swapped orientation epilogue: thread = feature row f, BN token columns in
 // chunks of 16, the next chunk's gathered operands loaded one chunk ahead.
 // Consecutive lanes hold consecutive features, so per-token stores coalesce.
@@ -530,7 +637,8 @@ __device__ __forceinline__ void epilogue_swap(const GemmDev& p, const EpiPre& e,
 template <int BN, int STAGES, int EPI, bool SWAP, int ACT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                   const __grid_constant__ CUtensorMap tmB, const GemmDev p) {
+                   const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, const GemmDev p) {
   constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
   constexpr int B_BYTES = BN * GEMM_BK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -540,15 +648,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // [ring][epilogue staging (1024-aligned; per-warp 4 KB TMA boxes or
+  // 32 x 33-word staging blocks)][column vectors][barriers]
+  uint32_t* stage_all = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES);
+  float* colv_all = reinterpret_cast<float*>(stage_all + 4 * 32 * STAGE_PITCH);  // [4][2][BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(colv_all + 4 * 2 * BN);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;   // [2]
   uint64_t* tempty = tfull + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  uint32_t* stage_all = reinterpret_cast<uint32_t*>(
-      smem + STAGES * STAGE_BYTES + 256);  // [4][32][STAGE_PITCH]
-  float* colv_all = reinterpret_cast<float*>(stage_all + 4 * 32 * STAGE_PITCH);  // [4][2][BN]
-  volatile int* fix_flag = reinterpret_cast<volatile int*>(colv_all + 4 * 2 * BN);
+  volatile int* fix_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -565,6 +674,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     fence_barrier_init();
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
+    if (p.tma_out) prefetch_tensormap(&tmO);
   }
   if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
@@ -705,6 +815,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         epilogue_swap<BN, EPI, ACT, false>(p, pre, taddr, nullptr,
                                            t.m0 + q * 32 + lane, t.nt * BN,
                                            lane);
+      else if (EPI != FVB_EPI_QKV_ROPE && p.tma_out)
+        epilogue_tma<BN, EPI, ACT>(p, &tmO, colv, taddr,
+                                   reinterpret_cast<uint8_t*>(stage_all) + q * 4096,
+                                   t.m0 + q * 32, t.nt * BN, lane);
       else
         epilogue_normal<BN, EPI, ACT>(p, pre, colv, taddr, stage, t.m0 + q * 32,
                                       t.nt * BN, lane);
@@ -712,6 +826,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (warp == 2 && lane == 0) trace_stamp(p, 11);
+    if (!SWAP && lane == 0) bulk_wait0();  // TMA stores complete before exit
+    if (warp == 2 && lane == 0) trace_stamp(p, 12);
     if (warp == 2 && lane == 0) trace_stamp(p, 6);
   }
   tc_fence_before();
@@ -728,7 +845,7 @@ template <int BN>
 struct GemmCfg {
   static constexpr int STAGES = (BN == 64) ? 8 : (BN == 128 ? 6 : 4);
   static constexpr int SMEM = STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) +
-                              1024 + 256 + 4 * 32 * STAGE_PITCH * 4 + 4 * 2 * BN * 4 + 16;
+                              1024 + 4 * 32 * STAGE_PITCH * 4 + 4 * 2 * BN * 4 + 256;
 };
 
 }  // namespace fvb

@@ -80,6 +80,53 @@ def test_gemm_f32_acc_gate(swap, split):
     torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
 
 
+@pytest.mark.parametrize('m,n,k,bn,split', [(130, 300, 592, 128, 3),
+                                            (3, 40, 64, 64, 1),
+                                            (768, 1152, 4304, 128, 2)])
+def test_gemm_f32_acc_ragged(m, n, k, bn, split):
+    """Ragged edge tiles of the TMA reduce-add epilogue (rows and columns
+    past the end are clipped by the tensor map)."""
+    torch.manual_seed(m + split)
+    x, w = rnd(m, k), rnd(n, k, std=0.02)
+    res = torch.randn(m, n, device=DEV)
+    bias = torch.randn(n, device=DEV) * 0.1
+    out = res.clone()
+    ops.gemm(x, w, out, epilogue=EPI_F32_ACC, bias=bias, split_k=split,
+             block_n=bn)
+    ref = res + x.float() @ w.float().t() + bias
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize('epi', [EPI_BF16, EPI_F32_STORE, EPI_F32_ACC])
+def test_gemm_unaligned_rows_write_back(epi):
+    """Output rows that do not start on 16-byte boundaries take the per-row
+    write-back instead of the TMA-store epilogue."""
+    torch.manual_seed(epi)
+    m, n, k = 200, 256, 256
+    x, w = rnd(m, k), rnd(n, k, std=0.02)
+    f32 = epi in (EPI_F32_STORE, EPI_F32_ACC)
+    cols = n
+    big = torch.randn(m, cols + 1, device=DEV)
+    if not f32:
+        big = big.bfloat16()
+    out = big[:, :cols]
+    before = out.clone()
+    edge = big[:, cols].clone()
+    ops.gemm(x, w, out, epilogue=epi)
+    acc = x.float() @ w.float().t()
+    if epi == EPI_F32_ACC:
+        ref = before + acc
+    else:
+        ref = acc
+    torch.cuda.synchronize()
+    if f32:
+        torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+    else:
+        close(out, ref)
+    assert torch.equal(big[:, cols], edge)  # the column past the view is untouched
+
+
 @pytest.mark.parametrize('swap', [False, True])
 def test_gemm_f32_store_row_add(swap):
     torch.manual_seed(4)
@@ -220,6 +267,51 @@ def test_attention_prefix_bidirectional_and_causal():
                     hd ** -0.5)
     torch.cuda.synchronize()
     close(o.view(E, H, hd).transpose(0, 1), ref)
+
+
+@pytest.mark.parametrize('case', ['growing_logits', 'masked_head_blocks',
+                                  'all_masked', 'gqa_ragged'])
+def test_attention_tensor_core_prefix(case):
+    """The tcgen05 prefill attention (unsplit, no suffix blocks): logits that
+    grow along the keys force the in-place O rescale; masked leading key
+    blocks start rows with no reference max; a fully masked prompt gives
+    zeros; 2 K/V heads with a ragged query count cover the flattened
+    (head, row) tiling."""
+    torch.manual_seed(10)
+    hd = 256
+    if case == 'gqa_ragged':
+        H, G, E = 4, 2, 100
+    else:
+        H, G, E = 8, 8, 816
+    KVH = H // G
+    q = rnd(E, H * hd)
+    k, v = rnd(E, KVH * hd), rnd(E, KVH * hd)
+    valid = torch.ones(E, dtype=torch.uint8, device=DEV)
+    if case == 'growing_logits':
+        k = (k.float() * (1 + 0.05 * torch.arange(E, device=DEV))[:, None]).bfloat16()
+    elif case == 'masked_head_blocks':
+        valid[:200] = 0
+        valid[700:] = 0
+    elif case == 'all_masked':
+        valid[:] = 0
+    o = torch.full_like(q, 7.0)
+    ops.attention(ops.attn_args(
+        q, k, v, o, n_q=E, n_kv=E, heads=H, group=G, head_dim=hd,
+        scale=hd ** -0.5, q_row_stride=H * hd, q_head_stride=hd,
+        k_row_stride=KVH * hd, k_head_stride=hd, v_row_stride=KVH * hd,
+        v_head_stride=hd, o_row_stride=H * hd, o_head_stride=hd,
+        key_valid=valid))
+    torch.cuda.synchronize()
+    got = o.view(E, H, hd).transpose(0, 1)
+    if case == 'all_masked':
+        assert torch.equal(got.float(), torch.zeros_like(got.float()))
+        return
+    for kh in range(KVH):
+        hs = slice(kh * G, (kh + 1) * G)
+        ref = _attn_ref(q.view(E, H, hd).transpose(0, 1)[hs],
+                        k[:, kh * hd:(kh + 1) * hd], v[:, kh * hd:(kh + 1) * hd],
+                        valid.bool()[None].expand(E, E), hd ** -0.5)
+        close(got[hs], ref)
 
 
 def test_attention_siglip_hd72_views():
