@@ -5,19 +5,25 @@
 // CTA = 128 query rows x all keys.  The rows of one K/V head's query group
 // are flattened (row r -> query head r / n_q, query row r % n_q), so with MQA
 // a tile spans heads and every CTA streams the shared K/V once.
-//   warps 0-3 : softmax; thread i owns query row i = TMEM lane i.  They
-//               stage Q (zero-padded to HDP columns) in shared memory, read
-//               S = Q K^T rows from TMEM, write P (bf16) to shared memory,
-//               and finally read O from TMEM, divide by the row sum, store.
-//   warp 4    : TMA producer, K and V tiles of 64 keys, double-buffered
-//               (boxes of 64 columns x 64 keys, 128-byte swizzle).
-//   warp 5    : allocates TMEM and issues the MMAs from one lane:
-//               S(j) = Q K_j^T  (M=128, N=64, K=HDP; both operands K-major)
+//   warps 0-7 : softmax.  Warp w owns TMEM lanes 32*(w%4).. (query rows)
+//               and key columns 32*(w/4).. of each 64-key block; the two
+//               warps of a row exchange row maxima (and at the end row sums)
+//               through shared memory.  They write Q (zero-padded to HDP)
+//               into TMEM, read S = Q K^T from TMEM, write P (bf16) back
+//               into the same TMEM columns, and finally read O, divide by
+//               the row sum and store.
+//   warp 8    : TMA producer of K tiles, warp 9 of V tiles (64 keys x 64
+//               columns per box, 128-byte swizzle), KS stages each.
+//   warp 10   : allocates TMEM and issues the MMAs from one lane, A operands
+//               from TMEM, B operands from shared memory:
+//               S(j) = Q K_j^T  (M=128, N=64, K=HDP; K tile K-major)
 //               O   += P_j V_j  (M=128, N=NV, K=64; V is [key][dim] in
 //               memory, i.e. MN-major for the B operand)
 //               S(j+1) is issued before O += P_j V_j so the softmax of block
-//               j overlaps the next QK^T.
-// TMEM: O in columns [0, NV), two S buffers of 64 columns after it.
+//               j overlaps the next QK^T.  MMAs of one thread execute in
+//               order, so S(j+2) overwriting the P(j) columns follows PV(j).
+// TMEM (32-bit columns): O [0, NV), S/P buffers 2 x 64, Q HDP/2 (bf16 pairs).
+// Keeping Q and P in TMEM leaves shared memory to the K/V pipeline.
 //
 // Online softmax with a lazily raised reference max: P = exp2(s - m_ref)
 // with m_ref the running row max, raised (and O, l rescaled in place) only
@@ -31,11 +37,12 @@
 #pragma once
 
 #include "common.cuh"
+#include "gemm_tc.cuh"  // g_gemm_trace (diagnostic stamps)
 
 namespace fvb {
 namespace atc {
 
-constexpr int BM = 128, BKV = 64, THREADS = 192;
+constexpr int BM = 128, BKV = 64, THREADS = 352;
 
 struct AtcDev {
   const bf16* q;
@@ -47,25 +54,33 @@ struct AtcDev {
   long long q_br, kv_br;
   float scale_log2;
   const uint8_t* key_valid;  // [n_kv] or null
+  int trace;                 // diagnostics: per-block stamps of CTA (0,0,0)
 };
+
+// keys per launch covered by the shared-memory validity bitmask
+constexpr int MAX_KEYS = 1024;
+constexpr int SOFTMAX_WARPS = 8;
 
 template <int HD, int HDP, int NV>
 struct AtcCfg {
   static_assert(HDP % 64 == 0 && HD <= HDP && NV % 16 == 0 && NV >= HD &&
                     NV <= 256,
                 "shape");
-  static constexpr int Q_BYTES = BM * HDP * 2;
   static constexpr int K_BYTES = BKV * HDP * 2;
   static constexpr int V_CHUNKS = (NV + 63) / 64;
   static constexpr int V_BYTES = BKV * V_CHUNKS * 128;
-  static constexpr int P_BYTES = BM * BKV * 2;
-  static constexpr int OFF_K = Q_BYTES;
-  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;
-  static constexpr uint32_t TMEM_S = NV <= 128 ? 128u : 256u;
-  static constexpr uint32_t TMEM_COLS = TMEM_S + 2 * BKV <= 256 ? 256u : 512u;
+  static constexpr int KS = (200 * 1024) / (K_BYTES + V_BYTES) < 4
+                                ? (200 * 1024) / (K_BYTES + V_BYTES) : 4;
+  static_assert(KS >= 2, "K/V stages");
+  static constexpr int OFF_V = KS * K_BYTES;
+  static constexpr int OFF_X = OFF_V + KS * V_BYTES;  // [2 parity][2 halves][BM] f32
+  static constexpr int OFF_MASK = OFF_X + 2 * 2 * BM * 4;
+  static constexpr int OFF_BAR = OFF_MASK + MAX_KEYS / 8;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;
+  static constexpr uint32_t TMEM_S = NV <= 128 ? 128u : 256u;  // 2 x BKV
+  static constexpr uint32_t TMEM_Q = TMEM_S + 2 * BKV;         // HDP / 2
+  static_assert(TMEM_Q + HDP / 2 <= 512, "TMEM");
+  static constexpr uint32_t TMEM_COLS = TMEM_Q + HDP / 2 <= 256 ? 256u : 512u;
 };
 
 // K-major SW128 descriptor = smem_desc_sw128.  MN-major SW128 (the V
@@ -83,21 +98,35 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t saddr,
   return d;
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 (A: lanes = rows, bf16
+// pairs along the columns).
+__device__ __forceinline__ void tc_mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a,
+                                               uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
       "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]),
-      "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
-      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
-      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
-      "r"(r[30]), "r"(r[31])
+      "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void atc_stamp(const AtcDev& p, int row, int slot) {
+  if (p.trace && row < 64 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    g_gemm_trace[row][slot] = globaltimer_ns();
 }
 
 template <int HD, int HDP, int NV>
@@ -105,50 +134,63 @@ __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AtcDev p) {
   using C = AtcCfg<HD, HDP, NV>;
+  constexpr int KS = C::KS;
   constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BKV);
   constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, NV) | (1u << 16);  // B MN-major
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sK = smem;
   uint8_t* sV = smem + C::OFF_V;
-  uint8_t* sP = smem + C::OFF_P;
+  float* sX = reinterpret_cast<float*>(smem + C::OFF_X);
+  uint32_t* sMask = reinterpret_cast<uint32_t*>(smem + C::OFF_MASK);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* k_empty = bars + 3;   // [2]
-  uint64_t* v_full = bars + 5;    // [2]
-  uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* s_free = bars + 11;   // [2]
-  uint64_t* p_full = bars + 13;   // [2]
-  uint64_t* o_done = bars + 15;   // [2]
-  uint64_t* o_final = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* k_full = bars;             // [KS]
+  uint64_t* k_empty = bars + KS;       // [KS]
+  uint64_t* v_full = bars + 2 * KS;    // [KS]
+  uint64_t* v_empty = bars + 3 * KS;   // [KS]
+  uint64_t* q_full = bars + 4 * KS;
+  uint64_t* s_full = q_full + 1;       // [2]
+  uint64_t* p_full = q_full + 3;       // [2]
+  uint64_t* o_done = q_full + 5;       // [2]
+  uint64_t* o_final = q_full + 7;
+  uint64_t* x_bar = q_full + 8;        // [2] row-max exchange, block j -> j&1
+  uint64_t* m_bar = q_full + 10;       // key bitmask built
+  uint64_t* l_bar = q_full + 11;       // row-sum exchange
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int nkb = (p.n_kv + BKV - 1) / BKV;
+  // Key blocks are visited in the order kb0, kb0+1, ... (mod nkb), kb0
+  // different per query tile, so the tiles of one K/V head do not all read
+  // the same K/V lines at the same moment (the online softmax does not
+  // depend on the order).
+  const int kb0 = tile % nkb;
+  auto key_block = [&](int j) { const int k = j + kb0; return k >= nkb ? k - nkb : k; };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 4);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < KS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
+    }
+    mbar_init(q_full, SOFTMAX_WARPS);
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 4);
-      mbar_init(&p_full[s], 4);
+      mbar_init(&p_full[s], SOFTMAX_WARPS);
       mbar_init(&o_done[s], 1);
+      mbar_init(&x_bar[s], SOFTMAX_WARPS);
     }
     mbar_init(o_final, 1);
+    mbar_init(m_bar, SOFTMAX_WARPS);
+    mbar_init(l_bar, SOFTMAX_WARPS);
     fence_barrier_init();
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
   }
-  if (warp == 5) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  if (warp == 10) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -156,200 +198,232 @@ __global__ void __launch_bounds__(THREADS, 1)
   griddep_wait();
   griddep_launch_dependents();
 
-  if (warp == 4) {
+  if (warp == 8 || warp == 9) {
+    // K (warp 8) or V (warp 9) producer
     if (lane == 0) {
+      const bool is_k = warp == 8;
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint8_t* dst = is_k ? sK : sV;
+      const int bytes = is_k ? C::K_BYTES : C::V_BYTES;
+      const int chunks = is_k ? HDP / 64 : C::V_CHUNKS;
+      const int x0 = kvh * (is_k ? p.k_hs : p.v_hs);
       const int y0 = (int)((long long)b * p.kv_br);
       for (int j = 0; j < nkb; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[s], ph ^ 1)) break;
-        mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
-#pragma unroll
-        for (int c = 0; c < HDP / 64; ++c)
-          tma_load_2d(sK + s * C::K_BYTES + c * BKV * 128, &tmK,
-                      kvh * p.k_hs + c * 64, y0 + j * BKV, &k_full[s]);
-        if (!mbar_wait(&v_empty[s], ph ^ 1)) break;
-        mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
-#pragma unroll
-        for (int c = 0; c < C::V_CHUNKS; ++c)
-          tma_load_2d(sV + s * C::V_BYTES + c * BKV * 128, &tmV,
-                      kvh * p.v_hs + c * 64, y0 + j * BKV, &v_full[s]);
+        const int s = j % KS;
+        if (!mbar_wait(&empty[s], ((j / KS) & 1) ^ 1)) break;
+        atc_stamp(p, j, is_k ? 6 : 7);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        for (int c = 0; c < chunks; ++c)
+          tma_load_2d(dst + s * bytes + c * BKV * 128, map, x0 + c * 64,
+                      y0 + key_block(j) * BKV, &full[s]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 10) {
     if (lane == 0) {
-      bool alive = mbar_wait(q_full, 0);
+      bool alive = mbar_wait_spin(q_full, 0);
+      atc_stamp(p, 63, 2);
       tc_fence_after();
-      const uint32_t q_base = smem_u32(sQ);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1)) return false;
-        if (j >= 2 && !mbar_wait(&s_free[s], ((j - 2) >> 1) & 1)) return false;
+        const int ks = j % KS, sb = j & 1;
+        if (!mbar_wait_spin(&k_full[ks], (j / KS) & 1)) return false;
+        if (j == 0) atc_stamp(p, 63, 3);
         tc_fence_after();
-        const uint32_t k_base = smem_u32(sK + s * C::K_BYTES);
-        const uint32_t d = tmem + C::TMEM_S + (uint32_t)(s * BKV);
+        const uint32_t k_base = smem_u32(sK + ks * C::K_BYTES);
+        const uint32_t d = tmem + C::TMEM_S + (uint32_t)(sb * BKV);
 #pragma unroll
-        for (int kk = 0; kk < HDP / 16; ++kk) {
-          const uint32_t off = (uint32_t)((kk & 3) * 32);
-          tc_mma_bf16(d, smem_desc_sw128(q_base + (kk >> 2) * (BM * 128) + off),
-                      smem_desc_sw128(k_base + (kk >> 2) * (BKV * 128) + off),
-                      IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(&s_full[s]);
-        tc_commit(&k_empty[s]);
+        for (int kk = 0; kk < HDP / 16; ++kk)
+          tc_mma_bf16_ts(d, tmem + C::TMEM_Q + (uint32_t)(kk * 8),
+                         smem_desc_sw128(k_base + (kk >> 2) * (BKV * 128) + (kk & 3) * 32),
+                         IDESC_S, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[sb]);
+        tc_commit(&k_empty[ks]);
+        atc_stamp(p, j, 4);
         return true;
       };
       if (alive) alive = issue_s(0);
       for (int j = 0; j < nkb && alive; ++j) {
         if (j + 1 < nkb && !(alive = issue_s(j + 1))) break;
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&p_full[s], ph) || !mbar_wait(&v_full[s], ph)) {
+        const int ks = j % KS, sb = j & 1;
+        if (!mbar_wait_spin(&p_full[sb], (j >> 1) & 1) ||
+            !mbar_wait_spin(&v_full[ks], (j / KS) & 1)) {
           alive = false;
           break;
         }
         tc_fence_after();
-        const uint32_t p_base = smem_u32(sP + s * C::P_BYTES);
-        const uint32_t v_base = smem_u32(sV + s * C::V_BYTES);
+        atc_stamp(p, j, 5);
+        const uint32_t v_base = smem_u32(sV + ks * C::V_BYTES);
+        const uint32_t p_cols = tmem + C::TMEM_S + (uint32_t)(sb * BKV);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          tc_mma_bf16(tmem, smem_desc_sw128(p_base + kk * 32),
-                      smem_desc_sw128_mn(v_base + kk * 2048, BKV * 128),
-                      IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&o_done[s]);
-        tc_commit(&v_empty[s]);
+          tc_mma_bf16_ts(tmem, p_cols + (uint32_t)(kk * 8),
+                         smem_desc_sw128_mn(v_base + kk * 2048, BKV * 128),
+                         IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&o_done[sb]);
+        tc_commit(&v_empty[ks]);
       }
       if (alive) tc_commit(o_final);
     }
   } else {
-    // ---- softmax warps: thread = query row i ----
-    const int i = warp * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // ---- softmax warps: query row i, key columns [32*hf, 32*hf + 32) ----
+    const int qd = warp & 3, hf = warp >> 2;
+    const int i = qd * 32 + lane;
+    const int tid = hf * BM + i;  // 0..255 over the softmax warps
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const int rows_total = p.group * p.n_q;
     const int r = tile * BM + i;
     const bool row_ok = r < rows_total;
     const int h = kvh * p.group + (row_ok ? r / p.n_q : 0);
     const int qrow = row_ok ? r % p.n_q : 0;
     {
+      // Q row i, bf16 pairs [hf*HDP/4, (hf+1)*HDP/4) -> TMEM columns
       const bf16* gq = p.q + ((long long)b * p.q_br + qrow) * p.q_rs + (long long)h * p.q_hs;
-      const uint32_t q_base = smem_u32(sQ);
-#pragma unroll 4
-      for (int c = 0; c < HDP / 8; ++c) {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (row_ok && c * 8 < HD) v = *reinterpret_cast<const uint4*>(gq + c * 8);
-        const int a = c >> 3, cc = c & 7;
-        const uint32_t addr = q_base + a * (BM * 128) + i * 128 + ((cc ^ (i & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                     : "memory");
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_full);
-    }
-    float m_ref = -INFINITY, l = 0.f;
-    bool alive = true;
-    const uint32_t p_row = (uint32_t)(i * 128);
-    for (int j = 0; j < nkb; ++j) {
-      const int s = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      // key validity of this block: bit t of kv[t / 32]
-      const int key0 = j * BKV;
-      uint32_t kv[2];
+      constexpr int QW = HDP / 4;  // 32-bit words of this half row
+#pragma unroll 1
+      for (int w0 = 0; w0 < QW; w0 += 16) {
+        uint32_t q[16];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int key = key0 + hh * 32 + lane;
-        bool ok = key < p.n_kv;
-        if (ok && p.key_valid) ok = p.key_valid[key] != 0;
-        kv[hh] = __ballot_sync(0xffffffffu, ok);
+        for (int u = 0; u < 4; ++u) {
+          const int e = (hf * QW + w0 + 4 * u) * 2;  // first element of the chunk
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (row_ok && e < HD) v = *reinterpret_cast<const uint4*>(gq + e);
+          q[4 * u] = v.x; q[4 * u + 1] = v.y; q[4 * u + 2] = v.z; q[4 * u + 3] = v.w;
+        }
+        tmem_st16(tmem + lane_base + C::TMEM_Q + (uint32_t)(hf * QW + w0), q);
       }
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], ph))) { alive = false; break; }
-      tc_fence_after();
-      uint32_t ra[32], rb[32];
-      tmem_ld32(tmem + lane_base + C::TMEM_S + (uint32_t)(s * BKV), ra);
-      tmem_ld32(tmem + lane_base + C::TMEM_S + (uint32_t)(s * BKV + 32), rb);
-      tmem_wait_ld32(ra);
-      tmem_wait_ld32(rb);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[s]);
-      float x[64];
-      float mx = -INFINITY;
+      if (lane == 0) mbar_arrive(q_full);
+      if (tid == 0) atc_stamp(p, 63, 0);
+    }
+    // key validity bitmask of all blocks (bit t of word w = key 32w + t)
+    for (int w = tid; w < nkb * 2; w += 2 * BM) {
+      uint32_t bits = 0;
+#pragma unroll 8
+      for (int t = 0; t < 32; ++t) {
+        const int key = w * 32 + t;
+        bool ok = key < p.n_kv;
+        if (ok && p.key_valid) ok = p.key_valid[key] != 0;
+        bits |= (ok ? 1u : 0u) << t;
+      }
+      sMask[w] = bits;
+    }
+    // the softmax warps exchange data through mbarriers with bounded waits
+    // (a warp that gives up cannot leave the others blocked)
+    __syncwarp();
+    if (lane == 0) mbar_arrive(m_bar);
+    bool alive = __all_sync(0xffffffffu, mbar_wait_spin(m_bar, 0));
+    if (tid == 0) atc_stamp(p, 63, 1);
+
+    float m_ref = -INFINITY, l = 0.f;
+    for (int j = 0; j < nkb && alive; ++j) {
+      const int sb = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      const uint32_t kv = sMask[2 * key_block(j) + hf];
+      const uint32_t s_cols = tmem + lane_base + C::TMEM_S + (uint32_t)(sb * BKV);
+      if (!__all_sync(0xffffffffu, mbar_wait_spin(&s_full[sb], ph))) { alive = false; break; }
+      tc_fence_after();
+      if (tid == 0) atc_stamp(p, j, 0);
+      uint32_t ra[32];
+      tmem_ld32(s_cols + (uint32_t)(hf * 32), ra);
+      tmem_wait_ld32(ra);
+      if (tid == 0) atc_stamp(p, j, 1);
+      float x[32];
+      float pm = -INFINITY;
 #pragma unroll
       for (int t = 0; t < 32; ++t) {
-        x[t] = ((kv[0] >> t) & 1u) ? __uint_as_float(ra[t]) * p.scale_log2 : -INFINITY;
-        x[32 + t] = ((kv[1] >> t) & 1u) ? __uint_as_float(rb[t]) * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, fmaxf(x[t], x[32 + t]));
+        x[t] = ((kv >> t) & 1u) ? __uint_as_float(ra[t]) * p.scale_log2 : -INFINITY;
+        pm = fmaxf(pm, x[t]);
       }
-      // raise the reference max (warp-uniform decision)
+      // row max over both column halves.  The P of this half is computed
+      // against the current reference while the exchange completes and is
+      // recomputed only if some row of the warp raises the reference.
+      // The arrive also orders this warp's S reads before the partner
+      // warp's P writes into the same columns.
+      float* xs = sX + sb * (2 * BM);
+      xs[hf * BM + i] = pm;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&x_bar[sb]);
+      uint32_t pw[16];
+      float rs = 0.f;
+      auto make_p = [&](float ref) {
+        const float base = (ref == -INFINITY) ? 0.f : ref;
+        rs = 0.f;
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const float p0 = exp2f(x[t] - base), p1 = exp2f(x[t + 1] - base);
+          rs += p0 + p1;
+          pw[t >> 1] = pack_bf16x2(p0, p1);
+        }
+      };
+      make_p(m_ref);  // block 0: recomputed below unless every key is masked
+      if (!__all_sync(0xffffffffu, mbar_wait_spin(&x_bar[sb], ph))) { alive = false; break; }
+      tc_fence_after();
+      const float mx = fmaxf(pm, xs[(hf ^ 1) * BM + i]);
+      // raise the reference max (warp-uniform decision; both warps of a row
+      // pair see the same maxima and decide alike)
       const bool raise = mx > m_ref + 8.f;
       if (__any_sync(0xffffffffu, raise)) {
         const float nref = raise ? mx : m_ref;
         const float alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - nref);
         if (j > 0) {
-          // O holds blocks < j: wait for the last PV, rescale in place
-          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) {
+          // O holds blocks < j: wait for the last PV, rescale this warp's
+          // 16-column chunks of O in place
+          if (!__all_sync(0xffffffffu, mbar_wait_spin(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) {
             alive = false;
             break;
           }
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < NV; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_base + (uint32_t)c, o);
-            tmem_wait_ld32(o);
+          for (int c = hf * 16; c < NV; c += 32) {
+            uint32_t o[16];
+            tmem_ld16_sync(tmem + lane_base + (uint32_t)c, o);
 #pragma unroll
-            for (int t = 0; t < 32; ++t)
+            for (int t = 0; t < 16; ++t)
               o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-            tmem_st32(tmem + lane_base + (uint32_t)c, o);
+            tmem_st16(tmem + lane_base + (uint32_t)c, o);
           }
-          tmem_wait_st();
         }
         l *= alpha;
         m_ref = nref;
-      }
-      const float base = (m_ref == -INFINITY) ? 0.f : m_ref;
-      uint32_t pw[32];
-      float rs = 0.f;
-#pragma unroll
-      for (int t = 0; t < 64; t += 2) {
-        const float p0 = exp2f(x[t] - base), p1 = exp2f(x[t + 1] - base);
-        rs += p0 + p1;
-        pw[t >> 1] = pack_bf16x2(p0, p1);
+        make_p(m_ref);
       }
       l += rs;
-      // P buffer s is free once PV(j-2) has completed
-      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&o_done[s], ((j - 2) >> 1) & 1))) {
-        alive = false;
-        break;
-      }
-      const uint32_t pb = smem_u32(sP + s * C::P_BYTES);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t addr = pb + p_row + ((c ^ (i & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr),
-                     "r"(pw[4 * c]), "r"(pw[4 * c + 1]), "r"(pw[4 * c + 2]),
-                     "r"(pw[4 * c + 3])
-                     : "memory");
-      }
-      fence_proxy_async_smem();
+      if (tid == 0) atc_stamp(p, j, 2);
+      // P (bf16 pairs, keys in order) over this half's S columns
+      tmem_st16(s_cols + (uint32_t)(hf * 16), pw);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[s]);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+      if (tid == 0) atc_stamp(p, j, 3);
     }
-    // ---- output: O / l ----
-    if (alive && __all_sync(0xffffffffu, mbar_wait(o_final, 0))) {
+    // ---- output: O / l, l summed over both column halves ----
+    // row sums go through the max-exchange slots of parity (nkb-1)^1: those
+    // were last read in block nkb-2, before every warp arrived on the
+    // exchange barrier of block nkb-1
+    float* ls = sX + (((nkb - 1) & 1) ^ 1) * (2 * BM);
+    if (alive) {
+      ls[hf * BM + i] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(l_bar);
+      alive = __all_sync(0xffffffffu, mbar_wait_spin(l_bar, 0));
+    }
+    const float lt = alive ? l + ls[(hf ^ 1) * BM + i] : 0.f;
+    if (alive && __all_sync(0xffffffffu, mbar_wait_spin(o_final, 0))) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
       bf16* go = p.o + ((long long)b * p.q_br + qrow) * p.o_rs + (long long)h * p.o_hs;
 #pragma unroll 1
-      for (int c = 0; c < NV; c += 32) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_base + (uint32_t)c, o);
-        tmem_wait_ld32(o);
+      for (int c = hf * 16; c < NV; c += 32) {
+        uint32_t o[16];
+        tmem_ld16_sync(tmem + lane_base + (uint32_t)c, o);
         if (row_ok) {
 #pragma unroll
-          for (int t = 0; t < 32; t += 8) {
+          for (int t = 0; t < 16; t += 8) {
             if (c + t < HD) {
               uint4 w;
               w.x = pack_bf16x2(__uint_as_float(o[t]) * inv, __uint_as_float(o[t + 1]) * inv);
@@ -365,7 +439,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 10) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }

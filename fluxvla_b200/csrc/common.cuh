@@ -86,6 +86,22 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t addr,
   return ok != 0;
 }
 
+// Latency-critical variant: polls with plain try_wait (no suspend hint), for
+// waits on a dependency chain that is short compared with a wake-up.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(addr, parity)) return true;
+    if (globaltimer_ns() - t0 > FVB_WAIT_LIMIT_NS) {
+      record_device_error(FVB_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Wait for the phase with the given parity to complete.  Returns false (and
 // records a device error) if it does not complete within FVB_WAIT_LIMIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {

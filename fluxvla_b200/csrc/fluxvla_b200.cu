@@ -175,6 +175,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
                   (size_t)C::SMEM, st, ma, mb, mo, d);
 }
 
+int g_trace_next = 0;
+
 // Tensor-core attention for unsplit attention without suffix block masks
 // (the SigLIP and Gemma prefix prefills); on unless FVB_ATTN_TC=0.
 bool attn_tc_enabled() {
@@ -208,6 +210,8 @@ int launch_attn_tc(const fvb_attn_args* a, const fvb::AttnDev& d,
   p.q_br = a->q_batch_rows; p.kv_br = a->kv_batch_rows;
   p.scale_log2 = d.scale_log2;
   p.key_valid = a->key_valid;
+  p.trace = g_trace_next;
+  g_trace_next = 0;
   auto kern = A::attn_tc_kernel<HD, HDP, NV>;
   static bool attr = false;
   if (!attr) {
@@ -222,7 +226,6 @@ int launch_attn_tc(const fvb_attn_args* a, const fvb::AttnDev& d,
                   dim3(A::THREADS), (size_t)C::SMEM, st, mk, mv, p);
 }
 
-int g_trace_next = 0;
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -484,7 +487,8 @@ int fvb_attention(const fvb_attn_args* a, void* stream) {
                   need);
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (d.splits == 1 && a->n_prefix >= a->n_kv && attn_tc_enabled() &&
+  if (d.splits == 1 && a->n_prefix >= a->n_kv && a->n_kv <= fvb::atc::MAX_KEYS &&
+      attn_tc_enabled() &&
       aligned16(a->o) && a->o_row_stride % 8 == 0 && a->o_head_stride % 8 == 0) {
     if (a->head_dim == 256) return launch_attn_tc<256, 256, 256>(a, d, st);
     return launch_attn_tc<72, 128, 80>(a, d, st);
