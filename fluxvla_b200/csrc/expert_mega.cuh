@@ -40,7 +40,7 @@ constexpr int MAX_KT = 8;                  // k-tiles per work item
 constexpr int APITCH = 264;                // attention smem row pitch (bf16)
 constexpr int ATILE = 64 * APITCH;         // elements per attention tile
 constexpr int REGION_BYTES = 3 * ATILE * 2 + 64 + 64 * 4 + 2 * 64 * 4;  // >= MAX_KT*BKT
-constexpr int SMEM_BYTES = 1024 + STAGES * A_BYTES + REGION_BYTES + 256;
+constexpr int SMEM_BYTES = 1024 + STAGES * A_BYTES + REGION_BYTES + 256 + TOK * 4;
 constexpr int N_GEMM = 4;  // QKV, O, GU, DOWN
 
 struct Gemm {
@@ -334,6 +334,13 @@ __device__ void attention_item(const Params& p, int layer, int item,
   bar128();  // the region is reused by the next item
 }
 
+// s_rstd[t] = 1/sqrt(ss[t]/width + eps) for the CTA (all worker threads sync)
+__device__ __forceinline__ void load_rstd(const Params& p, const float* ss,
+                                          float* s_rstd, int wtid) {
+  if (wtid < TOK) s_rstd[wtid] = rsqrtf(__ldcg(ss + min(wtid, p.n_tok - 1)) / p.width + p.eps);
+  bar128();
+}
+
 // xs[t,k] = bf16(x[t,k]*scale[k]) and ss[t] += sum_k x[t,k]^2, spread over
 // the grid (8 values per thread; a warp covers 256 values of one token)
 __device__ void prep_scaled(const Params& p, const float* scale, float* ss,
@@ -366,7 +373,8 @@ __device__ void prep_scaled(const Params& p, const float* scale, float* ss,
 }
 
 // hb[t,i] = bf16(gelu(rs*g + bg) * (rs*u + bu)), (g,u) = acc_gu[t, 2i..2i+1]
-__device__ void prep_geglu(const Params& p, const float* gub, int wtid) {
+__device__ void prep_geglu(const Params& p, const float* gub, const float* s_rstd,
+                           int wtid) {
   const int per_tok = p.mlp / 8;
   const int total = p.n_tok * per_tok;
   const int ld = 2 * p.mlp;
@@ -382,7 +390,7 @@ __device__ void prep_geglu(const Params& p, const float* gub, int wtid) {
       for (int h = 0; h < 4; ++h) q[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (c < total) {
         const int t = c / per_tok, i0 = (c % per_tok) * 8;
-        rs[u] = __ldcg(p.ss_post + t);
+        rs[u] = s_rstd[t];
         const float* src = p.acc_gu + (long long)t * ld + 2 * i0;
 #pragma unroll
         for (int h = 0; h < 4; ++h) q[u][h] = ldcg4(src + 4 * h);
@@ -393,7 +401,7 @@ __device__ void prep_geglu(const Params& p, const float* gub, int wtid) {
       const int c = base + u * gridDim.x * 128;
       if (c >= total) break;
       const int t = c / per_tok, i0 = (c % per_tok) * 8;
-      const float r = rsqrtf(rs[u] / p.width + p.eps);
+      const float r = rs[u];
       float y[8];
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
@@ -418,7 +426,7 @@ __device__ void prep_geglu(const Params& p, const float* gub, int wtid) {
 // the suffix tokens, written once as bf16 for every attention item.
 // Task (t, i): i < (H+1)*hd/2 is a rotary pair of a query head or the key
 // head, otherwise a pair (d, d + hd/2) of the value head.
-__device__ void finalize_qkv(const Params& p, int layer, int wtid) {
+__device__ void finalize_qkv(const Params& p, int layer, const float* s_rstd, int wtid) {
   const int H = p.heads, hd = p.hd, half = hd >> 1;
   const int qkv_ld = (H + 2) * hd;
   const int per_tok = (H + 2) * half;
@@ -436,7 +444,7 @@ __device__ void finalize_qkv(const Params& p, int layer, int wtid) {
       if (c < total) {
         const int t = c / per_tok, i = c % per_tok;
         const float* row = p.acc_qkv + (long long)t * qkv_ld;
-        rs[u] = __ldcg(p.ss_in + t);
+        rs[u] = s_rstd[t];
         if (i < (H + 1) * half) {
           const int hh = i / half, ii = i % half;
           a[u] = __ldcg(reinterpret_cast<const float2*>(row + hh * hd + 2 * ii));
@@ -454,7 +462,7 @@ __device__ void finalize_qkv(const Params& p, int layer, int wtid) {
       const int c = base + u * gridDim.x * 128;
       if (c >= total) break;
       const int t = c / per_tok, i = c % per_tok;
-      const float r = rsqrtf(rs[u] / p.width + p.eps);
+      const float r = rs[u];
       if (i < (H + 1) * half) {
         const int hh = i / half, ii = i % half;
         float x1 = r * a[u].x, x2 = r * a[u].y;
@@ -478,25 +486,31 @@ __device__ void finalize_qkv(const Params& p, int layer, int wtid) {
 
 // merge of the key-block partials of one (head, token) row -> attn (bf16)
 constexpr int MAX_NKB = 16;
-// merge of the key-block partials: task (head, token, 4 dims), spread over
-// the whole grid
+// merge of the key-block partials: task (head, token, 8 dims), spread over
+// the whole grid (one task per thread for the PI0 shapes)
 __device__ void merge_partials(const Params& p, int wtid) {
   const int S = p.n_tok, hd = p.hd;
-  const int quads = hd / 4;
-  const int total = p.heads * S * quads;
+  const int octs = hd / 8;
+  const int total = p.heads * S * octs;
   for (int c = blockIdx.x * 128 + wtid; c < total; c += gridDim.x * 128) {
-    const int row = c / quads, d = (c % quads) * 4;
+    const int row = c / octs, d = (c % octs) * 8;
     const int h = row / S, t = row % S;
     float2 ml[MAX_NKB];
-    float4 o[MAX_NKB];
 #pragma unroll
     for (int kb = 0; kb < MAX_NKB; ++kb) {
       ml[kb] = make_float2(-INFINITY, 0.f);
-      o[kb] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (kb < p.nkb)
+        ml[kb] = __ldcg(reinterpret_cast<const float2*>(
+            p.part_ml + (((long long)h * p.nkb + kb) * TOK + t) * 2));
+    }
+    float4 o0[MAX_NKB], o1[MAX_NKB];
+#pragma unroll
+    for (int kb = 0; kb < MAX_NKB; ++kb) {
+      o0[kb] = o1[kb] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (kb < p.nkb) {
-        const long long it = h * p.nkb + kb;
-        ml[kb] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (it * TOK + t) * 2));
-        o[kb] = ldcg4(p.part_o + (it * TOK + t) * hd + d);
+        const float* src = p.part_o + (((long long)h * p.nkb + kb) * TOK + t) * hd + d;
+        o0[kb] = ldcg4(src);
+        o1[kb] = ldcg4(src + 4);
       }
     }
     float M = -INFINITY;
@@ -504,19 +518,22 @@ __device__ void merge_partials(const Params& p, int wtid) {
     for (int kb = 0; kb < MAX_NKB; ++kb)
       if (ml[kb].y > 0.f) M = fmaxf(M, ml[kb].x);
     float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int kb = 0; kb < MAX_NKB; ++kb) {
       if (ml[kb].y > 0.f) {
         const float w = exp2f(ml[kb].x - M);
         L += w * ml[kb].y;
-        acc.x += w * o[kb].x; acc.y += w * o[kb].y;
-        acc.z += w * o[kb].z; acc.w += w * o[kb].w;
+        acc[0] += w * o0[kb].x; acc[1] += w * o0[kb].y;
+        acc[2] += w * o0[kb].z; acc[3] += w * o0[kb].w;
+        acc[4] += w * o1[kb].x; acc[5] += w * o1[kb].y;
+        acc[6] += w * o1[kb].z; acc[7] += w * o1[kb].w;
       }
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    *reinterpret_cast<uint2*>(p.attn + (long long)t * p.heads * hd + h * hd + d) =
-        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+    *reinterpret_cast<uint4*>(p.attn + (long long)t * p.heads * hd + h * hd + d) =
+        make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                   pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
   }
 }
 
@@ -543,6 +560,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* t_full = b_full + 1;
   uint64_t* t_empty = t_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 1);
+  // per-token rstd of the phase's RMSNorm, loaded once per CTA and phase:
+  // read per task from global memory, the whole grid would queue on the
+  // few L2 lines that hold the sums of squares
+  float* s_rstd = reinterpret_cast<float*>(region + REGION_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -650,7 +671,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (cta == 0 && wtid < TOK) p.ss_post[wtid] = 0.f;
           prep_scaled(p, p.in_scale + (long long)l * p.width, p.ss_in, wtid);
         } else if (ph == 2) {
-          finalize_qkv(p, l, wtid);
+          load_rstd(p, p.ss_in, s_rstd, wtid);
+          finalize_qkv(p, l, s_rstd, wtid);
         } else if (ph == 3) {
           for (int w = cta; w < p.heads * p.nkb; w += G)
             attention_item(p, l, w, region, wtid, false);
@@ -663,7 +685,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (ph == 6) {
           prep_scaled(p, p.post_scale + (long long)l * p.width, p.ss_post, wtid);
         } else if (ph == 8) {
-          prep_geglu(p, p.gu_bias ? p.gu_bias + (long long)l * 2 * p.mlp : nullptr, wtid);
+          load_rstd(p, p.ss_post, s_rstd, wtid);
+          prep_geglu(p, p.gu_bias ? p.gu_bias + (long long)l * 2 * p.mlp : nullptr, s_rstd,
+                     wtid);
         } else {
           const int gi = ph == 1 ? 0 : (ph == 5 ? 1 : (ph == 7 ? 2 : 3));
           const Gemm& g = p.g[gi];
