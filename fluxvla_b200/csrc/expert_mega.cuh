@@ -84,7 +84,7 @@ struct Params {
   bf16* xs;        // [TOK, width] x*(1+w) for the QKV / gate-up B operand
   bf16* hb;        // [TOK, mlp] gelu(g)*u for the down B operand
   bf16* kvs;       // [2][128, hd] suffix keys (rotated) / values (rows >= n_tok zero)
-  unsigned* bar;   // [0] count, [1] generation, [2] abort
+  unsigned* bar;   // [0..1] 64-bit arrival count, [BAR_ABORT] abort flag
   int nkb;         // key blocks of 64
   int trace;       // diagnostics: phase stamps of layer 0 in g_mega_trace
   int stages;      // weight ring depth in use (<= STAGES)
@@ -127,31 +127,31 @@ __device__ __forceinline__ void bar128() {
 }
 
 // Grid barrier among the 4 worker warps of every CTA: one acquire-release
-// arrival counter (bar[0]), a generation word (bar[BAR_GEN]) polled with
-// acquire loads, and the abort flag (bar[BAR_ABORT]) on its own line.
-constexpr int BAR_GEN = 32, BAR_ABORT = 288, BAR_WORDS = 320;
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* a) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+// 64-bit arrival counter (bar[0..1]) that only grows, polled with acquire
+// loads: the k-th barrier of the workspace's history completes when it
+// reaches (k+1)*gridDim.x, and each arrival learns k from the value it
+// replaced (64 bits: no wrap-around in any realistic lifetime).  The abort
+// flag bar[BAR_ABORT] is on its own line.
+constexpr int BAR_ABORT = 288, BAR_WORDS = 320;
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned* a) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
 }
-__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* a, unsigned v) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
-               : "=r"(old) : "l"(a), "r"(v) : "memory");
+__device__ __forceinline__ unsigned long long atom_add_acq_rel64(unsigned* a) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], 1;"
+               : "=l"(old) : "l"(a) : "memory");
   return old;
 }
 __device__ __forceinline__ void grid_sync(const Params& p, int wtid) {
   bar128();
   if (wtid == 0) {
-    // bar[0] only grows: the k-th barrier of the kernel's history completes
-    // when it reaches (k+1)*gridDim.x, and each arrival learns k from the
-    // value it replaced
-    const unsigned G = gridDim.x;
-    const unsigned old = atom_add_acq_rel(p.bar, 1u);
-    const unsigned target = (old / G + 1) * G;
+    const unsigned long long G = gridDim.x;
+    const unsigned long long old = atom_add_acq_rel64(p.bar);
+    const unsigned long long target = (old / G + 1) * G;
     uint64_t t0 = 0;
-    for (unsigned n = 0; (int)(ld_acquire(p.bar) - target) < 0; ++n) {
+    for (unsigned n = 0; ld_acquire64(p.bar) < target; ++n) {
       if ((n & 255) == 255) {
         if (aborted(p)) break;
         const uint64_t now = globaltimer_ns();
