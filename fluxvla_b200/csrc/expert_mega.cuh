@@ -77,7 +77,7 @@ struct Params {
   float* acc_gu;   // [TOK, 2*mlp]
   float* ss_in;    // [TOK]
   float* ss_post;  // [TOK]
-  float* part_o;   // [heads*nkb, TOK, hd]
+  float* part_o;   // [heads*nkb, TOK, hd] bf16, normalised per block
   float* part_ml;  // [heads*nkb, TOK, 2]
   bf16* attn;      // [TOK, heads*hd]
   bf16* qb;        // [TOK, heads*hd] rotated queries (rows >= n_tok zero)
@@ -227,6 +227,7 @@ __device__ void attention_item(const Params& p, int layer, int item,
   }
   cp_async_wait<0>();
   bar128();
+  if (tr) g_mega_trace[blockIdx.x][24] = globaltimer_ns();
 
   // S = Q K^T, masked online softmax over this block, O = P V
   const int warp = wtid >> 5, lane = wtid & 31;
@@ -291,8 +292,12 @@ __device__ void attention_item(const Params& p, int layer, int item,
     l0 += __shfl_xor_sync(0xffffffffu, l0, off);
     l1 += __shfl_xor_sync(0xffffffffu, l1, off);
   }
-  float* po = p.part_o + (long long)item * TOK * hd;
+  if (tr) g_mega_trace[blockIdx.x][25] = globaltimer_ns();
+  // partial output normalised by this block's row sum, as bf16 (the merge
+  // weights it back by the sum): half the bytes of an f32 partial
+  bf16* po = reinterpret_cast<bf16*>(p.part_o) + (long long)item * TOK * hd;
   float* pml = p.part_ml + (long long)item * TOK * 2;
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
   // P V in four 64-column passes to bound registers
 #pragma unroll 1
   for (int dp = 0; dp < 4; ++dp) {
@@ -320,17 +325,18 @@ __device__ void attention_item(const Params& p, int layer, int item,
     for (int nt = 0; nt < 8; ++nt) {
       const int d = dp * 64 + nt * 8 + (lane & 3) * 2;
       if (r0 < S)
-        __stcg(reinterpret_cast<float2*>(po + (long long)r0 * hd + d),
-               make_float2(o[nt][0], o[nt][1]));
+        __stcg(reinterpret_cast<unsigned*>(po + (long long)r0 * hd + d),
+               pack_bf16x2(o[nt][0] * inv0, o[nt][1] * inv0));
       if (r1 < S)
-        __stcg(reinterpret_cast<float2*>(po + (long long)r1 * hd + d),
-               make_float2(o[nt][2], o[nt][3]));
+        __stcg(reinterpret_cast<unsigned*>(po + (long long)r1 * hd + d),
+               pack_bf16x2(o[nt][2] * inv1, o[nt][3] * inv1));
     }
   }
   if ((lane & 3) == 0) {
     if (r0 < S) __stcg(reinterpret_cast<float2*>(pml + r0 * 2), make_float2(mx0, l0));
     if (r1 < S) __stcg(reinterpret_cast<float2*>(pml + r1 * 2), make_float2(mx1, l1));
   }
+  if (tr) g_mega_trace[blockIdx.x][26] = globaltimer_ns();
   bar128();  // the region is reused by the next item
 }
 
@@ -503,15 +509,14 @@ __device__ void merge_partials(const Params& p, int wtid) {
         ml[kb] = __ldcg(reinterpret_cast<const float2*>(
             p.part_ml + (((long long)h * p.nkb + kb) * TOK + t) * 2));
     }
-    float4 o0[MAX_NKB], o1[MAX_NKB];
+    uint4 o[MAX_NKB];
 #pragma unroll
     for (int kb = 0; kb < MAX_NKB; ++kb) {
-      o0[kb] = o1[kb] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (kb < p.nkb) {
-        const float* src = p.part_o + (((long long)h * p.nkb + kb) * TOK + t) * hd + d;
-        o0[kb] = ldcg4(src);
-        o1[kb] = ldcg4(src + 4);
-      }
+      o[kb] = make_uint4(0u, 0u, 0u, 0u);
+      if (kb < p.nkb)
+        o[kb] = __ldcg(reinterpret_cast<const uint4*>(
+            reinterpret_cast<const bf16*>(p.part_o) +
+            (((long long)h * p.nkb + kb) * TOK + t) * hd + d));
     }
     float M = -INFINITY;
 #pragma unroll
@@ -522,12 +527,15 @@ __device__ void merge_partials(const Params& p, int wtid) {
 #pragma unroll
     for (int kb = 0; kb < MAX_NKB; ++kb) {
       if (ml[kb].y > 0.f) {
-        const float w = exp2f(ml[kb].x - M);
-        L += w * ml[kb].y;
-        acc[0] += w * o0[kb].x; acc[1] += w * o0[kb].y;
-        acc[2] += w * o0[kb].z; acc[3] += w * o0[kb].w;
-        acc[4] += w * o1[kb].x; acc[5] += w * o1[kb].y;
-        acc[6] += w * o1[kb].z; acc[7] += w * o1[kb].w;
+        const float w = exp2f(ml[kb].x - M) * ml[kb].y;  // weight x block sum
+        L += w;
+        const uint32_t wd[4] = {o[kb].x, o[kb].y, o[kb].z, o[kb].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wd[e]));
+          acc[2 * e] += w * f.x;
+          acc[2 * e + 1] += w * f.y;
+        }
       }
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -675,7 +683,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           finalize_qkv(p, l, s_rstd, wtid);
         } else if (ph == 3) {
           for (int w = cta; w < p.heads * p.nkb; w += G)
-            attention_item(p, l, w, region, wtid, false);
+            attention_item(p, l, w, region, wtid, tr && l == 0 && w == cta);
         } else if (ph == 4) {  // merge; clear the QKV accumulators (read in ph 2)
           merge_partials(p, wtid);
           asm volatile("fence.proxy.async.global;" ::: "memory");
