@@ -330,8 +330,8 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
                 "fvb_gemm: output must be 16B aligned (QKV: n, head_dim "
                 "multiples of 32)");
   }
-  if (bn != 64 && bn != 128 && bn != 256)
-    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: block_n must be 64/128/256");
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: block_n must be 64/128/192/256");
 
   // K splits: F32_ACC adds atomically into its output; a swapped GEMM with
   // any other epilogue reduces its splits in the workspace
@@ -423,6 +423,7 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   if (a->swap) FVB_EPI_CASES(64, true)
   if (bn == 64) FVB_EPI_CASES(64, false)
   if (bn == 128) FVB_EPI_CASES(128, false)
+  if (bn == 192) FVB_EPI_CASES(192, false)
   FVB_EPI_CASES(256, false)
 #undef FVB_EPI_CASES
 }

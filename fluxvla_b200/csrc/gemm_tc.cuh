@@ -643,7 +643,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   constexpr int B_BYTES = BN * GEMM_BK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t IDESC = idesc_bf16_f32(GEMM_BM, BN);
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  // two accumulators; the allocation is a power of two >= 32 columns
+  constexpr uint32_t TMEM_COLS = 2 * BN <= 128 ? 2 * BN : (2 * BN <= 256 ? 256 : 512);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -843,7 +844,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int STAGES = (BN == 64) ? 8 : (BN == 128 ? 6 : 4);
+  static constexpr int STAGES = (BN == 64) ? 8 : (BN == 128 ? 6 : (BN == 192 ? 5 : 4));
   static constexpr int SMEM = STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) +
                               1024 + 4 * 32 * STAGE_PITCH * 4 + 4 * 2 * BN * 4 + 256;
 };

@@ -346,16 +346,16 @@ class PI0EngineB200:
             ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P[p + 'ln1_w'],
                      b=P[p + 'ln1_b'])
             ops.gemm(B['v_xn'], P[p + 'qkv_w'], qkv, bias=P[p + 'qkv_b'],
-                     block_n=256)
+                     block_n=192)
             ops.attention(attn)
             ops.gemm(B['v_ao'], P[p + 'o_w'], B['v_res'], epilogue=EPI_F32_ACC,
                      bias=P[p + 'o_b'], split_k=2)
             ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P[p + 'ln2_w'],
                      b=P[p + 'ln2_b'])
             ops.gemm(B['v_xn'], P[p + 'fc1_w'], B['v_h'], bias=P[p + 'fc1_b'],
-                     act=ACT_GELU_TANH, block_n=256)
+                     act=ACT_GELU_TANH, block_n=192)
             ops.gemm(B['v_h'], P[p + 'fc2_w'], B['v_res'], epilogue=EPI_F32_ACC,
-                     bias=P[p + 'fc2_b'], split_k=2)
+                     bias=P[p + 'fc2_b'], block_n=192, split_k=4)
         ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P['post_w'],
                  b=P['post_b'])
         ops.gemm(B['v_xn'], P['proj_w'], B['l_res'][:R], epilogue=EPI_F32_STORE,

@@ -63,7 +63,7 @@ typedef struct fvb_gemm_args {
   int32_t act;      /* FVB_ACT_*, FVB_EPI_BF16 only */
   int32_t split_k;  /* K splits: F32_ACC accumulates atomically into out;
                      * swapped non-additive epilogues need the workspace   */
-  int32_t block_n;  /* 0 = auto, else 64 / 128 / 256 */
+  int32_t block_n;  /* 0 = auto, else 64 / 128 / 192 / 256 */
   void* out;        /* see epilogues */
   int64_t ldo;      /* elements */
   const float* bias;    /* [features] or NULL */

@@ -30,7 +30,8 @@ def rnd(*s, std=1.0, dtype=torch.bfloat16):
 
 @pytest.mark.parametrize('m,n,k,bn', [(816, 2560, 2048, 128), (3, 40, 64, 0),
                                       (130, 300, 592, 64), (768, 4304, 1152, 256),
-                                      (17, 2048, 4304, 128)])
+                                      (17, 2048, 4304, 128), (768, 3456, 1152, 192),
+                                      (130, 300, 592, 192)])
 @pytest.mark.parametrize('act', [ACT_NONE, ACT_GELU_TANH])
 def test_gemm_bf16_bias_act(m, n, k, bn, act):
     torch.manual_seed(m + n)
@@ -82,7 +83,8 @@ def test_gemm_f32_acc_gate(swap, split):
 
 @pytest.mark.parametrize('m,n,k,bn,split', [(130, 300, 592, 128, 3),
                                             (3, 40, 64, 64, 1),
-                                            (768, 1152, 4304, 128, 2)])
+                                            (768, 1152, 4304, 128, 2),
+                                            (768, 1152, 4304, 192, 4)])
 def test_gemm_f32_acc_ragged(m, n, k, bn, split):
     """Ragged edge tiles of the TMA reduce-add epilogue (rows and columns
     past the end are clipped by the tensor map)."""
