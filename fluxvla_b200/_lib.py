@@ -30,7 +30,11 @@ class GemmArgs(C.Structure):
                 ('v_out', C.c_void_p), ('ld_kv', C.c_int64),
                 ('n_heads', C.c_int32), ('head_dim', C.c_int32),
                 ('rope_cs', C.c_void_p), ('positions', C.c_void_p),
-                ('workspace', C.c_void_p), ('workspace_bytes', C.c_int64)]
+                ('workspace', C.c_void_p), ('workspace_bytes', C.c_int64),
+                ('norm_mode', C.c_int32), ('norm_out', C.c_void_p),
+                ('ld_norm_out', C.c_int64), ('norm_w', C.c_void_p),
+                ('norm_b', C.c_void_p), ('norm_eps', C.c_float),
+                ('norm_sync', C.c_void_p)]
 
 
 class AttnArgs(C.Structure):

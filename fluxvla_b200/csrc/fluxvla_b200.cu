@@ -384,6 +384,26 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   d.trace = g_trace_next ? 1 : 0;
   g_trace_next = 0;
 
+  d.norm_out = reinterpret_cast<bf16*>(a->norm_out);
+  d.ld_norm_out = a->ld_norm_out;
+  d.norm_w = reinterpret_cast<const bf16*>(a->norm_w);
+  d.norm_b = reinterpret_cast<const bf16*>(a->norm_b);
+  d.norm_eps = a->norm_eps;
+  d.norm_mode = a->norm_mode;
+  d.norm_sync = reinterpret_cast<unsigned long long*>(a->norm_sync);
+  if (a->norm_out) {
+    const bool f32_out = a->epilogue == FVB_EPI_F32_ACC ||
+                         (a->epilogue == FVB_EPI_F32_STORE && !a->row_add);
+    if (a->swap || !f32_out || a->n % 128 || a->n > 2048 || a->ldo % 4 ||
+        !a->norm_w || !a->norm_sync || (reinterpret_cast<uintptr_t>(a->norm_sync) & 7) ||
+        (a->norm_mode != FVB_NORM_GEMMA_RMS && a->norm_mode != FVB_NORM_LAYER) ||
+        (a->norm_mode == FVB_NORM_LAYER && !a->norm_b) || a->ld_norm_out % 4 ||
+        (reinterpret_cast<uintptr_t>(a->norm_out) & 7) ||
+        (reinterpret_cast<uintptr_t>(a->norm_w) & 7) ||
+        (a->norm_b && (reinterpret_cast<uintptr_t>(a->norm_b) & 7)))
+      return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: unsupported fused norm arguments");
+  }
+
   // TMA-store epilogue: normal orientation, plain row-major output rows on
   // 16-byte boundaries (the position-embedding add and QKV+RoPE keep the
   // per-row write-back)

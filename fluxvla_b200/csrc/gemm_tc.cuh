@@ -60,7 +60,72 @@ struct GemmDev {
   int trace;  // diagnostics: record per-CTA phase times in g_gemm_trace
   int tma_out;  // normal orientation: the epilogue writes through the output
                 // tensor map (TMA store, or TMA f32 reduce-add for F32_ACC)
+  // fused norm of the finished f32 output rows (norm_out != null)
+  bf16* norm_out;
+  long long ld_norm_out;
+  const bf16* norm_w;
+  const bf16* norm_b;
+  float norm_eps;
+  int norm_mode;
+  unsigned long long* norm_sync;
 };
+
+// Arrivals of one launch at the fused-norm grid barrier add up to exactly
+// NORM_SYNC_UNIT (CTA 0 adds the part of the unit that the grid does not
+// fill), so the counter is shared by calls of any grid size.
+constexpr unsigned long long NORM_SYNC_UNIT = 4096;
+
+// Normalise one row of `dim` (<= 2048, multiple of 128) f32 values into
+// bf16: GEMMA_RMS x*rstd*(1+w) or LAYER (x-mean)*rstd*w + b.  One warp; the
+// row is read with L2 loads (written by other CTAs' TMA reductions).
+__device__ __forceinline__ void norm_row_warp(int mode, const float* xr, bf16* yr,
+                                              int dim, const bf16* w,
+                                              const bf16* b, float eps,
+                                              int lane) {
+  const int nv = dim >> 7;
+  float4 v[16];
+  float s = 0.f, ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < nv) v[i] = __ldcg(reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4));
+    s += v[i].x + v[i].y + v[i].z + v[i].w;
+    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  float mean = 0.f, rstd;
+  if (mode == FVB_NORM_LAYER) {
+    mean = warp_sum(s) / dim;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < nv)
+        q += (v[i].x - mean) * (v[i].x - mean) + (v[i].y - mean) * (v[i].y - mean) +
+             (v[i].z - mean) * (v[i].z - mean) + (v[i].w - mean) * (v[i].w - mean);
+    rstd = rsqrtf(warp_sum(q) / dim + eps);
+  } else {
+    rstd = rsqrtf(warp_sum(ss) / dim + eps);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i >= nv) break;
+    const int c0 = (i * 32 + lane) * 4;
+    const uint2 wq = *reinterpret_cast<const uint2*>(w + c0);
+    const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wq.x));
+    const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wq.y));
+    float y0 = (v[i].x - mean) * rstd, y1 = (v[i].y - mean) * rstd;
+    float y2 = (v[i].z - mean) * rstd, y3 = (v[i].w - mean) * rstd;
+    if (mode == FVB_NORM_LAYER) {
+      const uint2 bq = *reinterpret_cast<const uint2*>(b + c0);
+      const float2 b01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bq.x));
+      const float2 b23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bq.y));
+      y0 = y0 * w01.x + b01.x; y1 = y1 * w01.y + b01.y;
+      y2 = y2 * w23.x + b23.x; y3 = y3 * w23.y + b23.y;
+    } else {
+      y0 *= 1.f + w01.x; y1 *= 1.f + w01.y; y2 *= 1.f + w23.x; y3 *= 1.f + w23.y;
+    }
+    *reinterpret_cast<uint2*>(yr + c0) = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+  }
+}
 
 __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -839,6 +904,42 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
+  }
+  if (!SWAP && p.norm_out) {
+    // every CTA's output tiles are complete (TMA reductions waited above),
+    // then the CTAs normalise the finished rows, one warp per row
+    __threadfence();
+    __syncthreads();
+    volatile int* go = reinterpret_cast<volatile int*>(fix_flag);
+    if (threadIdx.x == 0) {
+      const unsigned long long add =
+          blockIdx.x == 0 ? NORM_SYNC_UNIT - gridDim.x + 1 : 1ull;
+      unsigned long long old;
+      asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;"
+                   : "=l"(old) : "l"(p.norm_sync), "l"(add) : "memory");
+      const unsigned long long target = (old / NORM_SYNC_UNIT + 1) * NORM_SYNC_UNIT;
+      bool ok = true;
+      const uint64_t t0 = globaltimer_ns();
+      for (unsigned n = 0;; ++n) {
+        unsigned long long v;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p.norm_sync) : "memory");
+        if (v >= target) break;
+        if ((n & 255) == 255 && globaltimer_ns() - t0 > FVB_WAIT_LIMIT_NS) {
+          record_device_error(FVB_ERR_DEVICE_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+      *go = ok;
+    }
+    __syncthreads();
+    if (*go) {
+      constexpr int NW = GEMM_THREADS / 32;
+      for (int row = blockIdx.x * NW + warp; row < p.m; row += gridDim.x * NW)
+        norm_row_warp(p.norm_mode, reinterpret_cast<const float*>(p.out) + (long long)row * p.ldo,
+                      p.norm_out + (long long)row * p.ld_norm_out, p.n, p.norm_w,
+                      p.norm_b, p.norm_eps, lane);
+    }
   }
 }
 

@@ -218,6 +218,8 @@ class PI0EngineB200:
                  ops.gemm_workspace_bytes(cfg.heads * hd + 2 * hd, S, True,
                                           EPI_QKV_ROPE))
         B['gemm_ws'] = z(ws, dt=torch.uint8)
+        # grid-barrier counter of the GEMMs with a fused norm (only grows)
+        B['norm_sync'] = z(1, dt=torch.int64)
         max_pos = E + S + 8
         B['rope'] = rope_table(max_pos, hd, device=d)
         B['rope_suffix'] = z(S, hd // 2, 2, dt=F32)
@@ -341,23 +343,27 @@ class PI0EngineB200:
             o_row_stride=Wv, o_head_stride=hdv, batch=cfg.n_views,
             q_batch_rows=cfg.tokens_per_view,
             kv_batch_rows=cfg.tokens_per_view)
+        # the LayerNorm after each residual GEMM runs in that GEMM's launch
+        # (fused norm behind a grid barrier); only the first one is separate
+        sync = B['norm_sync']
+        ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P['vision.l0.ln1_w'],
+                 b=P['vision.l0.ln1_b'])
         for i in range(cfg.vis_layers):
             p = f'vision.l{i}.'
-            ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P[p + 'ln1_w'],
-                     b=P[p + 'ln1_b'])
             ops.gemm(B['v_xn'], P[p + 'qkv_w'], qkv, bias=P[p + 'qkv_b'],
                      block_n=192)
             ops.attention(attn)
             ops.gemm(B['v_ao'], P[p + 'o_w'], B['v_res'], epilogue=EPI_F32_ACC,
-                     bias=P[p + 'o_b'], split_k=2)
-            ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P[p + 'ln2_w'],
-                     b=P[p + 'ln2_b'])
+                     bias=P[p + 'o_b'], split_k=2,
+                     norm=(NORM_LAYER, B['v_xn'], P[p + 'ln2_w'], P[p + 'ln2_b'],
+                           1e-6, sync))
             ops.gemm(B['v_xn'], P[p + 'fc1_w'], B['v_h'], bias=P[p + 'fc1_b'],
                      act=ACT_GELU_TANH, block_n=192)
+            nxt = f'vision.l{i + 1}.ln1_' if i + 1 < cfg.vis_layers else 'post_'
             ops.gemm(B['v_h'], P[p + 'fc2_w'], B['v_res'], epilogue=EPI_F32_ACC,
-                     bias=P[p + 'fc2_b'], block_n=192, split_k=4)
-        ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P['post_w'],
-                 b=P['post_b'])
+                     bias=P[p + 'fc2_b'], block_n=192, split_k=4,
+                     norm=(NORM_LAYER, B['v_xn'], P[nxt + 'w'], P[nxt + 'b'],
+                           1e-6, sync))
         ops.gemm(B['v_xn'], P['proj_w'], B['l_res'][:R], epilogue=EPI_F32_STORE,
                  bias=P['proj_b'])
 
@@ -367,10 +373,11 @@ class PI0EngineB200:
         R = cfg.n_views * cfg.tokens_per_view if self.has_vision else 0
         ops.embed_tokens(B['tokens'][:E - R], P['embed'],
                          math.sqrt(cfg.llm_width), B['l_res'][R:])
+        sync = B['norm_sync']
+        ops.norm(NORM_GEMMA_RMS, B['l_res'], B['l_xn'], w=P['llm.l0.in_norm'])
         for i in range(cfg.llm_layers):
             p = f'llm.l{i}.'
             kc, vc = B['kc'][i], B['vc'][i]
-            ops.norm(NORM_GEMMA_RMS, B['l_res'], B['l_xn'], w=P[p + 'in_norm'])
             ops.gemm(B['l_xn'], P[p + 'qkv'], B['l_q'], epilogue=EPI_QKV_ROPE,
                      k_out=kc[:E], v_out=vc[:E], n_heads=H, head_dim=hd,
                      rope_cs=B['rope'], positions=B['pos_prefix'])
@@ -383,13 +390,16 @@ class PI0EngineB200:
                 v_row_stride=hd, v_head_stride=0, o_row_stride=H * hd,
                 o_head_stride=hd, key_valid=B['key_valid'], n_prefix=E))
             ops.gemm(B['l_ao'], P[p + 'o_w'], B['l_res'], epilogue=EPI_F32_ACC,
-                     block_n=256, split_k=2)
-            ops.norm(NORM_GEMMA_RMS, B['l_res'], B['l_xn'],
-                     w=P[p + 'post_norm'])
+                     block_n=256, split_k=2,
+                     norm=(NORM_GEMMA_RMS, B['l_xn'], P[p + 'post_norm'], None,
+                           1e-6, sync))
             ops.gemm(B['l_xn'], P[p + 'gu'], B['l_h'], epilogue=EPI_GEGLU,
                      block_n=256)
+            # the next layer's input norm rides on the down projection
             ops.gemm(B['l_h'], P[p + 'down_w'], B['l_res'],
-                     epilogue=EPI_F32_ACC, block_n=256, split_k=5)
+                     epilogue=EPI_F32_ACC, block_n=256, split_k=5,
+                     norm=(NORM_GEMMA_RMS, B['l_xn'], P[f'llm.l{i + 1}.in_norm'],
+                           None, 1e-6, sync))
 
     def _state_token(self):
         if self.cfg.has_state_token:

@@ -47,11 +47,15 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
          v_out: Optional[torch.Tensor] = None, n_heads: int = 0,
          head_dim: int = 0, rope_cs: Optional[torch.Tensor] = None,
          positions: Optional[torch.Tensor] = None,
-         workspace: Optional[torch.Tensor] = None) -> None:
+         workspace: Optional[torch.Tensor] = None,
+         norm: Optional[tuple] = None) -> None:
     """C[M,N] = A[M,K] @ B[N,K]^T with a fused epilogue (see fvb_gemm).
     split_k=0 picks the split automatically for swapped GEMMs; a swapped
     split GEMM with a non-additive epilogue needs ``workspace`` (a zeroed
-    uint8 tensor of gemm_workspace_bytes(...), left zeroed by the call)."""
+    uint8 tensor of gemm_workspace_bytes(...), left zeroed by the call).
+    ``norm=(mode, out_bf16, w, b, eps, sync)`` normalises the finished f32
+    output rows into ``out_bf16`` in the same launch (``sync``: an int64
+    device tensor, zero before first use)."""
     lda = _rowmajor(a, 'a', BF16)
     ldb = _rowmajor(b, 'b', BF16)
     if a.shape[1] != b.shape[1]:
@@ -73,6 +77,14 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
                     positions=_ptr(positions), workspace=_ptr(workspace),
                     workspace_bytes=0 if workspace is None else
                     workspace.numel() * workspace.element_size())
+    if norm is not None:
+        mode, nout, nw, nb, eps, sync = norm
+        args.norm_mode = mode
+        args.norm_out = _ptr(nout)
+        args.ld_norm_out = _rowmajor(nout, 'norm_out', BF16)
+        args.norm_w, args.norm_b = _ptr(nw), _ptr(nb)
+        args.norm_eps = eps
+        args.norm_sync = _ptr(sync)
     check(_lib.lib().fvb_gemm(C.byref(args), _stream()))
 
 

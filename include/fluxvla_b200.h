@@ -91,6 +91,23 @@ typedef struct fvb_gemm_args {
    * (enough tiles to fill the GPU) for swapped GEMMs.                       */
   void* workspace;
   int64_t workspace_bytes;
+  /* Optional fused norm of the finished output, on when norm_out != NULL
+   * (normal orientation, FVB_EPI_F32_ACC or FVB_EPI_F32_STORE without
+   * row_add): once every output tile of the call is written (a grid-wide
+   * barrier on norm_sync), the CTAs normalise the rows of out into norm_out
+   * (bf16 [m, ld_norm_out]) with FVB_NORM_GEMMA_RMS (norm_w) or
+   * FVB_NORM_LAYER (norm_w, norm_b), bf16 weights [n], n a multiple of 128
+   * and <= 2048.  norm_sync: 8 bytes of device memory, zero before the first
+   * use, advanced (never reset) by every call; calls sharing it must not
+   * overlap on the GPU.  This replaces the residual GEMM + norm kernel pair
+   * between two layers' GEMMs.                                              */
+  int32_t norm_mode; /* FVB_NORM_GEMMA_RMS or FVB_NORM_LAYER */
+  void* norm_out;
+  int64_t ld_norm_out;
+  const void* norm_w;
+  const void* norm_b;
+  float norm_eps;
+  void* norm_sync;
 } fvb_gemm_args;
 
 /* tcgen05/TMEM tensor-core GEMM with fused epilogues.

@@ -24,7 +24,7 @@ def _act(x, act):
 def gemm(a, b, out, *, epilogue=EPI_BF16, swap=False, act=0, bias=None,
          gate=None, alpha=1.0, split_k=1, block_n=0, row_add=None,
          row_add_mod=0, k_out=None, v_out=None, n_heads=0, head_dim=0,
-         rope_cs=None, positions=None, workspace=None):
+         rope_cs=None, positions=None, workspace=None, norm=None):
     _count[0] += 1
     acc = a.float() @ b.float().t()
     if swap:
@@ -59,6 +59,9 @@ def gemm(a, b, out, *, epilogue=EPI_BF16, swap=False, act=0, bias=None,
         out.copy_(r[:, :H].reshape(T, H * hd).to(out.dtype))
         k_out.copy_(r[:, H].to(k_out.dtype))
         v_out.copy_(acc[:, (H + 1) * hd:].to(v_out.dtype))
+    if norm is not None:  # fused norm of the finished output, same launch
+        mode, nout, nw, nb, eps, _sync = norm
+        _norm_into(mode, out, nout, nw, nb, None, eps)
 
 
 class _Args:
@@ -124,6 +127,10 @@ def gemm_workspace_bytes(m, n, swap, epilogue):
 
 def norm(mode, x, out, *, w=None, b=None, mod=None, eps=1e-6):
     _count[0] += 1
+    _norm_into(mode, x, out, w, b, mod, eps)
+
+
+def _norm_into(mode, x, out, w, b, mod, eps):
     D = x.shape[1]
     if mode == NORM_LAYER:
         y = F.layer_norm(x, (D,), w.float(), b.float(), eps)

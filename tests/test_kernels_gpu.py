@@ -129,6 +129,33 @@ def test_gemm_unaligned_rows_write_back(epi):
     assert torch.equal(big[:, cols], edge)  # the column past the view is untouched
 
 
+@pytest.mark.parametrize('mode,m,n,k,bn,split', [
+    (NORM_GEMMA_RMS, 816, 2048, 2048, 256, 2),
+    (NORM_LAYER, 768, 1152, 4304, 192, 4),
+    (NORM_LAYER, 100, 1152, 256, 128, 1)])
+def test_gemm_fused_residual_norm(mode, m, n, k, bn, split):
+    """Residual GEMM with the next norm fused behind a grid-wide barrier:
+    out += x w^T, then norm(out) -> bf16, twice on one sync counter."""
+    torch.manual_seed(m + n)
+    sync = torch.zeros(1, dtype=torch.int64, device=DEV)
+    for it in range(2):
+        x, w = rnd(m, k), rnd(n, k, std=0.02)
+        res = torch.randn(m, n, device=DEV)
+        nw, nb = rnd(n, std=0.5), rnd(n, std=0.5)
+        out = res.clone()
+        xn = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+        ops.gemm(x, w, out, epilogue=EPI_F32_ACC, split_k=split, block_n=bn,
+                 norm=(mode, xn, nw, nb if mode == NORM_LAYER else None, 1e-6, sync))
+        ref = res + x.float() @ w.float().t()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+        if mode == NORM_LAYER:
+            yref = torch.nn.functional.layer_norm(ref, (n,), nw.float(), nb.float(), 1e-6)
+        else:
+            yref = ref * torch.rsqrt(ref.pow(2).mean(-1, keepdim=True) + 1e-6) * (1 + nw.float())
+        close(xn, yref)
+
+
 @pytest.mark.parametrize('swap', [False, True])
 def test_gemm_f32_store_row_add(swap):
     torch.manual_seed(4)
