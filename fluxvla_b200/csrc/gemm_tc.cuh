@@ -946,6 +946,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 template <int BN>
 struct GemmCfg {
   static constexpr int STAGES = (BN == 64) ? 8 : (BN == 128 ? 6 : (BN == 192 ? 5 : 4));
+  static_assert(BN % 32 == 0 && BN <= 256, "block_n");
   static constexpr int SMEM = STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) +
                               1024 + 4 * 32 * STAGE_PITCH * 4 + 4 * 2 * BN * 4 + 256;
 };

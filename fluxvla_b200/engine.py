@@ -425,10 +425,11 @@ class PI0EngineB200:
             ops.gemm(P['action_time_in_w'][:, :We], B['a_emb'], B['at_h'],
                      swap=True, bias=self.step_bias[k], act=ACT_SILU,
                      split_k=0, workspace=B['gemm_ws'])
-            res.zero_()
+            # K splits summed in the workspace, the last split stores
             ops.gemm(P['action_time_out_w'], B['at_h'], res[off:],
-                     epilogue=EPI_F32_ACC, swap=True,
-                     bias=P['action_time_out_b'], split_k=0)
+                     epilogue=EPI_F32_STORE, swap=True,
+                     bias=P['action_time_out_b'], split_k=0,
+                     workspace=B['gemm_ws'])
             if off:
                 res[:off].copy_(B['state_emb'])
         if self.loop_impl == 'mega':
