@@ -349,12 +349,16 @@ def run_b200(args):
                  for n in ('qkv', 'o_w', 'gu', 'down_w'))
     kvbytes = 2 * L * E * cfg.head_dim * 2
     ach = (wbytes + kvbytes) / t_launch / 1e9
+    # DRAM bytes (read + write) of one launch, from an ncu capture of this
+    # launch on the full config (dram__bytes_read.sum + dram__bytes_write.sum
+    # = 640.4 + 3.3 MB; PI0 / PI0.5 geometry, E = 816)
+    traffic = 643.7e6 if (L == 18 and E == 816 and not args.depth) else None
     roof = {'kernel': f'fvb::mega::expert_step_kernel ({L} expert layers of one '
                       'denoise step, persistent, 148 CTAs)',
             'bound': 'hbm', 'achieved': ach, 'peak': peaks['hbm_gbs'],
             'unit': 'GB/s', 'frac': ach / peaks['hbm_gbs'],
             'peak_source': f'{peak_kind} HBM copy (kernel timed alone)',
-            'traffic': None, 'launch_us': t_launch * 1e6,
+            'traffic': traffic, 'launch_us': t_launch * 1e6,
             'algorithmic_bytes_per_launch': wbytes + kvbytes}
     roof_prefill = None
     if w != 'loop':
