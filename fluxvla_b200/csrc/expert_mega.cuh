@@ -720,6 +720,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_2d(region + i * BKT_BYTES, bmap, (kt0 + i) * 64, 0, b_full);
               }
             }
+            // the lane that issued goes first: spinning lanes of a diverged
+            // warp can otherwise hold it off
+            __syncwarp();
             // epilogue: thread = weight row (output feature), 64 token columns
             const bool ok = wait_bar(p, t_full, j & 1);
             __syncwarp();
