@@ -345,7 +345,6 @@ class PI0EngineB200:
             kv_batch_rows=cfg.tokens_per_view)
         # the LayerNorm after each residual GEMM runs in that GEMM's launch
         # (fused norm behind a grid barrier); only the first one is separate
-        sync = B['norm_sync']
         ops.norm(NORM_LAYER, B['v_res'], B['v_xn'], w=P['vision.l0.ln1_w'],
                  b=P['vision.l0.ln1_b'])
         for i in range(cfg.vis_layers):
@@ -353,19 +352,35 @@ class PI0EngineB200:
             ops.gemm(B['v_xn'], P[p + 'qkv_w'], qkv, bias=P[p + 'qkv_b'],
                      block_n=192)
             ops.attention(attn)
-            ops.gemm(B['v_ao'], P[p + 'o_w'], B['v_res'], epilogue=EPI_F32_ACC,
-                     bias=P[p + 'o_b'], split_k=2,
-                     norm=(NORM_LAYER, B['v_xn'], P[p + 'ln2_w'], P[p + 'ln2_b'],
-                           1e-6, sync))
+            self._residual_gemm('vis_o', B['v_ao'], P[p + 'o_w'], B['v_res'],
+                                dict(bias=P[p + 'o_b'], split_k=2),
+                                (NORM_LAYER, B['v_xn'], P[p + 'ln2_w'], P[p + 'ln2_b']))
             ops.gemm(B['v_xn'], P[p + 'fc1_w'], B['v_h'], bias=P[p + 'fc1_b'],
                      act=ACT_GELU_TANH, block_n=192)
             nxt = f'vision.l{i + 1}.ln1_' if i + 1 < cfg.vis_layers else 'post_'
-            ops.gemm(B['v_h'], P[p + 'fc2_w'], B['v_res'], epilogue=EPI_F32_ACC,
-                     bias=P[p + 'fc2_b'], block_n=192, split_k=4,
-                     norm=(NORM_LAYER, B['v_xn'], P[nxt + 'w'], P[nxt + 'b'],
-                           1e-6, sync))
+            self._residual_gemm('vis_fc2', B['v_h'], P[p + 'fc2_w'], B['v_res'],
+                                dict(bias=P[p + 'fc2_b'], block_n=192, split_k=4),
+                                (NORM_LAYER, B['v_xn'], P[nxt + 'w'], P[nxt + 'b']))
         ops.gemm(B['v_xn'], P['proj_w'], B['l_res'][:R], epilogue=EPI_F32_STORE,
                  bias=P['proj_b'])
+
+    # residual GEMM call sites whose following norm runs in the GEMM's launch
+    # (grid barrier + norm tail); the others launch the norm kernel after it.
+    # None by default: measured on the full prefill (5.45 ms unfused vs
+    # 5.71 ms with all four sites fused), the grid barrier holds every CTA
+    # until the slowest tile is done, which costs more than the norm launch
+    # whose start overlaps the GEMM's tail under programmatic dependent launch.
+    fused_norm_sites = frozenset()
+
+    def _residual_gemm(self, site, a, w, res, kw, norm):
+        """res += a @ w^T, then norm(res) -> bf16 (mode, out, w, b)."""
+        mode, out, nw, nb = norm
+        if site in self.fused_norm_sites:
+            ops.gemm(a, w, res, epilogue=EPI_F32_ACC,
+                     norm=(mode, out, nw, nb, 1e-6, self.B['norm_sync']), **kw)
+        else:
+            ops.gemm(a, w, res, epilogue=EPI_F32_ACC, **kw)
+            ops.norm(mode, res, out, w=nw, b=nb)
 
     def _llm(self):
         cfg, P, B, E = self.cfg, self.P, self.B, self.E
@@ -373,7 +388,6 @@ class PI0EngineB200:
         R = cfg.n_views * cfg.tokens_per_view if self.has_vision else 0
         ops.embed_tokens(B['tokens'][:E - R], P['embed'],
                          math.sqrt(cfg.llm_width), B['l_res'][R:])
-        sync = B['norm_sync']
         ops.norm(NORM_GEMMA_RMS, B['l_res'], B['l_xn'], w=P['llm.l0.in_norm'])
         for i in range(cfg.llm_layers):
             p = f'llm.l{i}.'
@@ -389,17 +403,16 @@ class PI0EngineB200:
                 q_head_stride=hd, k_row_stride=hd, k_head_stride=0,
                 v_row_stride=hd, v_head_stride=0, o_row_stride=H * hd,
                 o_head_stride=hd, key_valid=B['key_valid'], n_prefix=E))
-            ops.gemm(B['l_ao'], P[p + 'o_w'], B['l_res'], epilogue=EPI_F32_ACC,
-                     block_n=256, split_k=2,
-                     norm=(NORM_GEMMA_RMS, B['l_xn'], P[p + 'post_norm'], None,
-                           1e-6, sync))
+            self._residual_gemm('llm_o', B['l_ao'], P[p + 'o_w'], B['l_res'],
+                                dict(block_n=256, split_k=2),
+                                (NORM_GEMMA_RMS, B['l_xn'], P[p + 'post_norm'], None))
             ops.gemm(B['l_xn'], P[p + 'gu'], B['l_h'], epilogue=EPI_GEGLU,
                      block_n=256)
             # the next layer's input norm rides on the down projection
-            ops.gemm(B['l_h'], P[p + 'down_w'], B['l_res'],
-                     epilogue=EPI_F32_ACC, block_n=256, split_k=5,
-                     norm=(NORM_GEMMA_RMS, B['l_xn'], P[f'llm.l{i + 1}.in_norm'],
-                           None, 1e-6, sync))
+            self._residual_gemm('llm_down', B['l_h'], P[p + 'down_w'], B['l_res'],
+                                dict(block_n=256, split_k=5),
+                                (NORM_GEMMA_RMS, B['l_xn'],
+                                 P[f'llm.l{i + 1}.in_norm'], None))
 
     def _state_token(self):
         if self.cfg.has_state_token:
