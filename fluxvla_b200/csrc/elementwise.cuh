@@ -209,4 +209,92 @@ __global__ void small_linear_kernel(const float* __restrict__ x, long long ldx,
   }
 }
 
+
+__device__ __forceinline__ float small_linear_finish(float acc, const float* bias,
+                                                     int n, int act) {
+  float y = acc + (bias ? bias[n] : 0.f);
+  if (act == FVB_ACT_SILU) y = silu_f(y);
+  else if (act == FVB_ACT_GELU_TANH) y = gelu_tanh_f(y);
+  return y;
+}
+
+__device__ __forceinline__ void small_linear_store(void* out, long long ldo, int t,
+                                                   int n, int mode, float alpha,
+                                                   float y) {
+  if (mode == 0)
+    reinterpret_cast<float*>(out)[(long long)t * ldo + n] = y;
+  else if (mode == 1)
+    reinterpret_cast<bf16*>(out)[(long long)t * ldo + n] = __float2bfloat16(y);
+  else
+    reinterpret_cast<float*>(out)[(long long)t * ldo + n] += alpha * y;
+}
+
+// Narrow K (<= 64, multiple of 8; the action / state input projections):
+// one thread per output, the weight row read as 16-byte vectors, the token
+// row staged once per block in shared memory.  Block = one token x 256
+// outputs.
+__global__ void __launch_bounds__(256)
+    small_linear_narrow_kernel(const float* __restrict__ x, long long ldx, int K,
+                               const bf16* __restrict__ w, long long ldw, int N,
+                               const float* __restrict__ bias, int act, int mode,
+                               float alpha, void* out, long long ldo) {
+  __shared__ float xs[64];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int chunks = (N + 255) / 256;
+  const int t = blockIdx.x / chunks;
+  const int n = (blockIdx.x % chunks) * 256 + threadIdx.x;
+  if (threadIdx.x < K) xs[threadIdx.x] = x[(long long)t * ldx + threadIdx.x];
+  __syncthreads();
+  if (n >= N) return;
+  const uint4* wr = reinterpret_cast<const uint4*>(w + (long long)n * ldw);
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c * 8 >= K) break;
+    const uint4 q = __ldg(wr + c);
+    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wd[e]));
+      acc += xs[c * 8 + 2 * e] * f.x + xs[c * 8 + 2 * e + 1] * f.y;
+    }
+  }
+  small_linear_store(out, ldo, t, n, mode, alpha, small_linear_finish(acc, bias, n, act));
+}
+
+// Wide K (multiple of 256, <= 4096; the action output projection): one warp
+// per output, every lane loading 16-byte weight vectors and two float4 of
+// the token row per 256-wide step, all steps' loads in flight together.
+__global__ void __launch_bounds__(256)
+    small_linear_wide_kernel(const float* __restrict__ x, long long ldx, int T,
+                             int K, const bf16* __restrict__ w, long long ldw,
+                             int N, const float* __restrict__ bias, int act,
+                             int mode, float alpha, void* out, long long ldo) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= T * N) return;
+  const int t = gw / N, n = gw % N;
+  const float* xr = x + (long long)t * ldx + lane * 8;
+  const bf16* wr = w + (long long)n * ldw + lane * 8;
+  float acc = 0.f;
+#pragma unroll 4
+  for (int k = 0; k < K; k += 256) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(wr + k));
+    const float4 a = *reinterpret_cast<const float4*>(xr + k);
+    const float4 b = *reinterpret_cast<const float4*>(xr + k + 4);
+    const float2 w0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+    const float2 w1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+    const float2 w2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.z));
+    const float2 w3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.w));
+    acc += a.x * w0.x + a.y * w0.y + a.z * w1.x + a.w * w1.y +
+           b.x * w2.x + b.y * w2.y + b.z * w3.x + b.w * w3.y;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0)
+    small_linear_store(out, ldo, t, n, mode, alpha, small_linear_finish(acc, bias, n, act));
+}
+
 }  // namespace fvb

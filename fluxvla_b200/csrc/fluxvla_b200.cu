@@ -626,6 +626,19 @@ int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
                      int64_t ldo, void* stream) {
   if (!x || !w || !out || t <= 0 || k <= 0 || n <= 0 || mode < 0 || mode > 2)
     return fail(FVB_ERR_INVALID_ARG, "fvb_small_linear: bad arguments");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = aligned16(w) && ldw % 8 == 0;
+  if (vec && k % 8 == 0 && k <= 64)
+    return launch_k("fvb_small_linear", fvb::small_linear_narrow_kernel,
+                    dim3((unsigned)((long long)t * ((n + 255) / 256))), dim3(256), 0, st,
+                    x, (long long)ldx, (int)k, (const bf16*)w, (long long)ldw,
+                    (int)n, bias, (int)act, (int)mode, alpha, out, (long long)ldo);
+  if (vec && k % 256 == 0 && aligned16(x) && ldx % 4 == 0)
+    return launch_k("fvb_small_linear", fvb::small_linear_wide_kernel,
+                    dim3((unsigned)(((long long)t * n * 32 + 255) / 256)), dim3(256), 0,
+                    st, x, (long long)ldx, (int)t, (int)k, (const bf16*)w,
+                    (long long)ldw, (int)n, bias, (int)act, (int)mode, alpha, out,
+                    (long long)ldo);
   const long long warps = (long long)t * n;
   const int threads = 256;
   const long long blocks = (warps * 32 + threads - 1) / threads;

@@ -421,6 +421,41 @@ def test_patchify_embed_small_linear():
     torch.testing.assert_close(acc, ref, atol=1e-4, rtol=1e-4)
 
 
+@pytest.mark.parametrize('T,K,N,mode,act,xoff', [
+    (50, 32, 1024, 1, ACT_NONE, 0),      # narrow K, bf16 out (action in-proj)
+    (1, 32, 1024, 0, ACT_NONE, 0),       # state token
+    (50, 1024, 32, 2, ACT_NONE, 0),      # wide K, x += alpha * y (out-proj)
+    (7, 1024, 100, 0, ACT_SILU, 0),      # wide K, f32 out with activation
+    (5, 40, 33, 0, ACT_NONE, 0),         # narrow K, ragged N
+    (3, 300, 17, 0, ACT_GELU_TANH, 1)])  # generic path (K not a multiple of 256, unaligned x)
+def test_small_linear_paths(T, K, N, mode, act, xoff):
+    torch.manual_seed(T * K + N)
+    xb = torch.randn(T, K + xoff, device=DEV)
+    x = xb[:, xoff:]
+    w = rnd(N, K, std=0.1)
+    bias = torch.randn(N, device=DEV)
+    y = x @ w.float().t() + bias
+    if act == ACT_SILU:
+        y = torch.nn.functional.silu(y)
+    elif act == ACT_GELU_TANH:
+        y = torch.nn.functional.gelu(y, approximate='tanh')
+    if mode == 1:
+        out = torch.empty(T, N, device=DEV, dtype=torch.bfloat16)
+        ref = y
+    elif mode == 2:
+        out = torch.randn(T, N, device=DEV)
+        ref = out + 0.25 * y
+    else:
+        out = torch.empty(T, N, device=DEV)
+        ref = y
+    ops.small_linear(x, w, out, bias=bias, mode=mode, alpha=0.25, act=act)
+    torch.cuda.synchronize()
+    if mode == 1:
+        close(out, ref)
+    else:
+        torch.testing.assert_close(out, ref, atol=1e-3, rtol=1e-3)
+
+
 @pytest.mark.parametrize('split', [0, 3, 16])
 def test_gemm_swap_split_fixup(split):
     """Swapped split-K GEMMs with non-additive epilogues reduce their splits
