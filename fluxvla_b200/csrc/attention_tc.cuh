@@ -55,6 +55,12 @@ struct AtcDev {
   float scale_log2;
   const uint8_t* key_valid;  // [n_kv] or null
   int trace;                 // diagnostics: per-block stamps of CTA (0,0,0)
+  // split over keys (splits > 1): blockIdx.z = batch * splits + split covers
+  // key blocks [split * blocks_per_split, ...) and writes its un-normalised
+  // partial (O f32, max, sum) for attn_combine_kernel
+  int heads, splits, blocks_per_split;
+  float* part_o;   // [splits][batch*heads*n_q][HD]
+  float* part_ml;  // [splits][batch*heads*n_q][2]
 };
 
 // keys per launch covered by the shared-memory validity bitmask
@@ -119,14 +125,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int nkb = (p.n_kv + BKV - 1) / BKV;
+  const int tile = blockIdx.x, kvh = blockIdx.y;
+  const int b = blockIdx.z / p.splits, split = blockIdx.z % p.splits;
+  const int nkb_all = (p.n_kv + BKV - 1) / BKV;
+  const int kb_begin = split * p.blocks_per_split;
+  const int nkb = min(p.blocks_per_split, nkb_all - kb_begin);  // this CTA's blocks
   // Key blocks are visited in the order kb0, kb0+1, ... (mod nkb), kb0
   // different per query tile, so the tiles of one K/V head do not all read
   // the same K/V lines at the same moment (the online softmax does not
   // depend on the order).
   const int kb0 = tile % nkb;
-  auto key_block = [&](int j) { const int k = j + kb0; return k >= nkb ? k - nkb : k; };
+  auto key_block = [&](int j) {
+    const int k = j + kb0;
+    return kb_begin + (k >= nkb ? k - nkb : k);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < KS; ++s) {
@@ -258,7 +270,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (tid == 0) atc_stamp(p, 63, 0);
     }
     // key validity bitmask of all blocks (bit t of word w = key 32w + t)
-    for (int w = tid; w < nkb * 2; w += 2 * BM) {
+    for (int w = tid; w < nkb_all * 2; w += 2 * BM) {
       uint32_t bits = 0;
 #pragma unroll 8
       for (int t = 0; t < 32; ++t) {
@@ -372,7 +384,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       alive = __all_sync(0xffffffffu, mbar_wait_spin(l_bar, 0));
     }
     const float lt = alive ? l + ls[(hf ^ 1) * BM + i] : 0.f;
-    if (alive && __all_sync(0xffffffffu, mbar_wait_spin(o_final, 0))) {
+    if (alive && p.splits > 1 && __all_sync(0xffffffffu, mbar_wait_spin(o_final, 0))) {
+      // partial: O relative to m_ref (f32), (m_ref, row sum)
+      tc_fence_after();
+      const long long rows = (long long)gridDim.z / p.splits * p.heads * p.n_q;
+      const long long row = ((long long)b * p.heads + h) * p.n_q + qrow;
+      float* po = p.part_o + ((long long)split * rows + row) * HD;
+#pragma unroll 1
+      for (int c = hf * 16; c < NV; c += 32) {
+        uint32_t o[16];
+        tmem_ld16_sync(tmem + lane_base + (uint32_t)c, o);
+        if (row_ok) {
+#pragma unroll
+          for (int t = 0; t < 16; t += 4)
+            if (c + t < HD)
+              *reinterpret_cast<float4*>(po + c + t) =
+                  make_float4(__uint_as_float(o[t]), __uint_as_float(o[t + 1]),
+                              __uint_as_float(o[t + 2]), __uint_as_float(o[t + 3]));
+        }
+      }
+      if (row_ok && hf == 0)
+        *reinterpret_cast<float2*>(p.part_ml + ((long long)split * rows + row) * 2) =
+            make_float2(m_ref, lt);
+    } else if (alive && __all_sync(0xffffffffu, mbar_wait_spin(o_final, 0))) {
       tc_fence_after();
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
       bf16* go = p.o + ((long long)b * p.q_br + qrow) * p.o_rs + (long long)h * p.o_hs;

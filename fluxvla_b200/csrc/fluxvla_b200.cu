@@ -210,6 +210,11 @@ int launch_attn_tc(const fvb_attn_args* a, const fvb::AttnDev& d,
   p.q_br = a->q_batch_rows; p.kv_br = a->kv_batch_rows;
   p.scale_log2 = d.scale_log2;
   p.key_valid = a->key_valid;
+  p.heads = a->heads;
+  p.splits = d.splits;
+  p.blocks_per_split = d.blocks_per_split;
+  p.part_o = d.part_o;
+  p.part_ml = d.part_ml;
   p.trace = g_trace_next;
   g_trace_next = 0;
   auto kern = A::attn_tc_kernel<HD, HDP, NV>;
@@ -222,7 +227,8 @@ int launch_attn_tc(const fvb_attn_args* a, const fvb::AttnDev& d,
     attr = true;
   }
   const int tiles = (a->group * a->n_q + A::BM - 1) / A::BM;
-  return launch_k("fvb_attention", kern, dim3(tiles, a->heads / a->group, a->batch),
+  return launch_k("fvb_attention", kern,
+                  dim3(tiles, a->heads / a->group, a->batch * d.splits),
                   dim3(A::THREADS), (size_t)C::SMEM, st, mk, mv, p);
 }
 
@@ -508,7 +514,7 @@ int fvb_attention(const fvb_attn_args* a, void* stream) {
                   need);
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (d.splits == 1 && a->n_prefix >= a->n_kv && a->n_kv <= fvb::atc::MAX_KEYS &&
+  if (a->n_prefix >= a->n_kv && a->n_kv <= fvb::atc::MAX_KEYS &&
       attn_tc_enabled() &&
       aligned16(a->o) && a->o_row_stride % 8 == 0 && a->o_head_stride % 8 == 0) {
     if (a->head_dim == 256) return launch_attn_tc<256, 256, 256>(a, d, st);

@@ -220,6 +220,10 @@ class PI0EngineB200:
         B['gemm_ws'] = z(ws, dt=torch.uint8)
         # grid-barrier counter of the GEMMs with a fused norm (only grows)
         B['norm_sync'] = z(1, dt=torch.int64)
+        # key-split partials of the prefix attention (f32 O + max/sum),
+        # sized for up to 4 splits
+        B['prefix_attn_ws'] = z(4 * cfg.heads * E * (hd + 2) * 4 + 16,
+                                dt=torch.uint8)
         max_pos = E + S + 8
         B['rope'] = rope_table(max_pos, hd, device=d)
         B['rope_suffix'] = z(S, hd // 2, 2, dt=F32)
@@ -371,6 +375,10 @@ class PI0EngineB200:
     # until the slowest tile is done, which costs more than the norm launch
     # whose start overlaps the GEMM's tail under programmatic dependent launch.
     fused_norm_sites = frozenset()
+    # key splits of the Gemma prefix attention (tcgen05 kernel + combine).
+    # 1: measured on the full prefill, 2 splits (102 CTAs + the combine of
+    # f32 partials) cost 0.2 ms more than 51 unsplit CTAs
+    prefix_attn_splits = 1
 
     def _residual_gemm(self, site, a, w, res, kw, norm):
         """res += a @ w^T, then norm(res) -> bf16 (mode, out, w, b)."""
@@ -402,7 +410,8 @@ class PI0EngineB200:
                 head_dim=hd, scale=hd ** -0.5, q_row_stride=H * hd,
                 q_head_stride=hd, k_row_stride=hd, k_head_stride=0,
                 v_row_stride=hd, v_head_stride=0, o_row_stride=H * hd,
-                o_head_stride=hd, key_valid=B['key_valid'], n_prefix=E))
+                o_head_stride=hd, key_valid=B['key_valid'], n_prefix=E,
+                kv_splits=self.prefix_attn_splits, workspace=B['prefix_attn_ws']))
             self._residual_gemm('llm_o', B['l_ao'], P[p + 'o_w'], B['l_res'],
                                 dict(block_n=256, split_k=2),
                                 (NORM_GEMMA_RMS, B['l_xn'], P[p + 'post_norm'], None))

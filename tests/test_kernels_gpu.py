@@ -298,9 +298,10 @@ def test_attention_prefix_bidirectional_and_causal():
     close(o.view(E, H, hd).transpose(0, 1), ref)
 
 
+@pytest.mark.parametrize('splits', [1, 2, 3])
 @pytest.mark.parametrize('case', ['growing_logits', 'masked_head_blocks',
                                   'all_masked', 'gqa_ragged'])
-def test_attention_tensor_core_prefix(case):
+def test_attention_tensor_core_prefix(case, splits):
     """The tcgen05 prefill attention (unsplit, no suffix blocks): logits that
     grow along the keys force the in-place O rescale; masked leading key
     blocks start rows with no reference max; a fully masked prompt gives
@@ -324,12 +325,15 @@ def test_attention_tensor_core_prefix(case):
     elif case == 'all_masked':
         valid[:] = 0
     o = torch.full_like(q, 7.0)
-    ops.attention(ops.attn_args(
-        q, k, v, o, n_q=E, n_kv=E, heads=H, group=G, head_dim=hd,
-        scale=hd ** -0.5, q_row_stride=H * hd, q_head_stride=hd,
-        k_row_stride=KVH * hd, k_head_stride=hd, v_row_stride=KVH * hd,
-        v_head_stride=hd, o_row_stride=H * hd, o_head_stride=hd,
-        key_valid=valid))
+    kw = dict(n_q=E, n_kv=E, heads=H, group=G, head_dim=hd,
+              scale=hd ** -0.5, q_row_stride=H * hd, q_head_stride=hd,
+              k_row_stride=KVH * hd, k_head_stride=hd, v_row_stride=KVH * hd,
+              v_head_stride=hd, o_row_stride=H * hd, o_head_stride=hd,
+              key_valid=valid, kv_splits=splits)
+    args = ops.attn_args(q, k, v, o, **kw)
+    ws = torch.empty(max(ops.attention_workspace_bytes(args), 16),
+                     dtype=torch.uint8, device=DEV)
+    ops.attention(ops.attn_args(q, k, v, o, workspace=ws, **kw))
     torch.cuda.synchronize()
     got = o.view(E, H, hd).transpose(0, 1)
     if case == 'all_masked':
