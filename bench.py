@@ -258,6 +258,9 @@ def run_b200(args):
     del W
     torch.cuda.empty_cache()
 
+    if w == 'serve':
+        return run_serve(args, cfg, eng, n_tok, E, world, rank, local, dev)
+
     g = torch.Generator().manual_seed(1 + rank)
     imgs = torch.randint(0, 256, (cfg.n_views, 224, 224, 3), generator=g,
                          dtype=torch.uint8).pin_memory()
@@ -422,6 +425,59 @@ def run_b200(args):
     return 0
 
 
+def run_serve(args, cfg, eng, n_tok, E, world, rank, local, dev):
+    """config[4]: batches of independent config[2] requests (seeded per
+    request) sharded round-robin over one replica per GPU; aggregate
+    chunks/s and per-request p50/p99 latency (wall clock from the batch's
+    release to the request's actions on the host, queueing included)."""
+    import torch.distributed as dist
+
+    from fluxvla_b200.serving import (ReplicaServer, dist_helpers,
+                                      make_request, sweep)
+    batches = [int(b) for b in args.batches.split(',') if b]
+    server = ReplicaServer(eng)
+    barrier, gather = dist_helpers(world, dev)
+    cache = {}
+
+    def request_of(i):
+        if i not in cache:
+            cache[i] = make_request(cfg, n_tok, i, seed_base=1000)
+        return cache[i]
+    # capture + warm-up on this rank's first request
+    for _ in range(args.warmup):
+        server.serve([request_of(rank)], 0.0)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.6)
+    res = sweep(server, request_of, batches, rank, world, barrier, gather)
+    clocks = sampler.stop() if sampler else None
+    if rank == 0:
+        top = res[-1]
+        print(json.dumps({
+            'metric': 'PI0 serving sweep (config[4]): aggregate chunks/s and '
+                      'p50/p99 request latency',
+            'value': top['chunks_per_s'], 'unit': 'chunks/s', 'n_gpus': world,
+            'steps': len(batches), 'warmup': args.warmup,
+            'ms_per_step': 1000.0 * world / top['chunks_per_s'],
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+            'dtype': 'bf16',
+            'data': 'synthetic (seeded random bf16 weights; inputs seeded per '
+                    'request = 1000 + index)',
+            'config': {'workload': 'config[4]: PI0 serving sweep, config[2] '
+                                   'requests, round-robin over one replica '
+                                   'per GPU', 'batches': batches,
+                       'prefix_rows': E, 'parallelism': f'replicas{world}'},
+            'sweep': res, 'clocks': clocks,
+            'gpu_launches': int(eng.launches_per_call *
+                                sum(r['requests_per_gpu'] for r in res)),
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -429,7 +485,9 @@ def main():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--workload', default='pi0',
-                    choices=['pi0', 'pi05', 'loop'])
+                    choices=['pi0', 'pi05', 'loop', 'serve'])
+    ap.add_argument('--batches', default='1,4,16,64',
+                    help='serve workload: batch sizes of the sweep')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--depth', type=int, default=0,
                     help='profiling only: layers per tower (0 = full model)')
