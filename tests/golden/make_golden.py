@@ -232,72 +232,9 @@ def build_ref_model(ref, cfg: PI0Config):
 
 
 def name_map(cfg: PI0Config):
-    """our weight name -> reference state_dict key."""
-    m = {'vision.patch_w':
-         'vision_backbone.vision.vision_model.embeddings.patch_embedding.weight',
-         'vision.patch_b':
-         'vision_backbone.vision.vision_model.embeddings.patch_embedding.bias',
-         'vision.pos': 'vision_backbone.vision.vision_model.embeddings.'
-         'position_embedding.weight',
-         'vision.post_w':
-         'vision_backbone.vision.vision_model.post_layernorm.weight',
-         'vision.post_b':
-         'vision_backbone.vision.vision_model.post_layernorm.bias',
-         'proj_w': 'projector.projector.weight',
-         'proj_b': 'projector.projector.bias',
-         'llm.embed': 'llm_backbone.embed_tokens.weight',
-         'llm.norm': 'llm_backbone.norm.weight',
-         'action_in_w': 'action_in_proj.projector.weight',
-         'action_in_b': 'action_in_proj.projector.bias',
-         'action_out_w': 'action_out_proj.projector.weight',
-         'action_out_b': 'action_out_proj.projector.bias'}
-    for i in range(cfg.vis_layers):
-        s = f'vision_backbone.vision.vision_model.encoder.layers.{i}.'
-        p = f'vision.l{i}.'
-        for a, b in [('ln1', 'layer_norm1'), ('ln2', 'layer_norm2')]:
-            m[p + a + '_w'] = s + b + '.weight'
-            m[p + a + '_b'] = s + b + '.bias'
-        for a, b in [('q', 'q_proj'), ('k', 'k_proj'), ('v', 'v_proj'),
-                     ('o', 'out_proj')]:
-            m[p + a + '_w'] = s + 'self_attn.' + b + '.weight'
-            m[p + a + '_b'] = s + 'self_attn.' + b + '.bias'
-        for a in ['fc1', 'fc2']:
-            m[p + a + '_w'] = s + 'mlp.' + a + '.weight'
-            m[p + a + '_b'] = s + 'mlp.' + a + '.bias'
-
-    def gemma(ours, theirs, layers, ada):
-        for i in range(layers):
-            s, p = f'{theirs}.layers.{i}.', f'{ours}l{i}.'
-            for a in 'qkvo':
-                m[p + a + '_w'] = s + f'self_attn.{a}_proj.weight'
-            for a in ['gate', 'up', 'down']:
-                m[p + a + '_w'] = s + f'mlp.{a}_proj.weight'
-            for a, b in [('in_norm', 'input_layernorm'),
-                         ('post_norm', 'post_attention_layernorm')]:
-                if ada:
-                    m[p + a + '_dense_w'] = s + b + '.dense.weight'
-                    m[p + a + '_dense_b'] = s + b + '.dense.bias'
-                else:
-                    m[p + a] = s + b + '.weight'
-        if ada:
-            m[ours + 'norm_dense_w'] = theirs + '.norm.dense.weight'
-            m[ours + 'norm_dense_b'] = theirs + '.norm.dense.bias'
-        else:
-            m[ours + 'norm'] = theirs + '.norm.weight'
-
-    gemma('llm.', 'llm_backbone', cfg.llm_layers, False)
-    gemma('exp.', 'llm_expert', cfg.exp_layers, cfg.adarms)
-    if cfg.adarms:
-        for a in ['in', 'out']:
-            m[f'time_{a}_w'] = f'time_mlp_{a}.projector.weight'
-            m[f'time_{a}_b'] = f'time_mlp_{a}.projector.bias'
-    else:
-        m['state_proj_w'] = 'state_proj.projector.weight'
-        m['state_proj_b'] = 'state_proj.projector.bias'
-        for a in ['in', 'out']:
-            m[f'action_time_{a}_w'] = f'action_time_mlp_{a}.projector.weight'
-            m[f'action_time_{a}_b'] = f'action_time_mlp_{a}.projector.bias'
-    return m
+    """our weight name -> reference state_dict key (the product's map)."""
+    from fluxvla_b200.loader import reference_name_map
+    return reference_name_map(cfg)
 
 
 def load_weights(model, cfg, W):
