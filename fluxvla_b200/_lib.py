@@ -84,6 +84,10 @@ EXPORTS = {
                            C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
                            C.c_void_p]),
+    'fvb_resize_patchify': (C.c_int, [C.c_void_p, C.c_int32, C.c_int32,
+                                      C.c_int32, C.c_int32, C.c_int32,
+                                      C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_int64, C.c_void_p]),
     'fvb_patchify': (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                C.c_int32, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_int64, C.c_void_p]),

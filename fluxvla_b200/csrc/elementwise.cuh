@@ -138,6 +138,64 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// One axis of OpenCV's INTER_LINEAR resize: taps s0, s1 and 11-bit
+// fixed-point weights of destination index d (f computed in double without
+// contraction, rounded to float, weights rounded half to even).  Along x a
+// tap outside [0, src-1) has its fraction forced to 0; along y only the row
+// indices are clamped.
+__device__ __forceinline__ void resize_taps(int d, int dst, int src, bool clamp_w,
+                                            int& s0, int& s1, int& w0, int& w1) {
+  const double scale = __drcp_rn(__ddiv_rn((double)dst, (double)src));
+  float f = (float)__dadd_rn(__dmul_rn((double)d + 0.5, scale), -0.5);
+  int s = (int)floorf(f);
+  f -= (float)s;
+  if (clamp_w) {
+    if (s < 0) { s = 0; f = 0.f; }
+    if (s >= src - 1) { s = src - 1; f = 0.f; }
+  }
+  w0 = (int)rintf(__fmul_rn(1.f - f, 2048.f));
+  w1 = (int)rintf(__fmul_rn(f, 2048.f));
+  s0 = min(max(s, 0), src - 1);
+  s1 = min(max(s + 1, 0), src - 1);
+}
+
+// uint8 HWC views of any size -> resized (OpenCV INTER_LINEAR, bit-exact
+// uint8) -> normalised -> bf16 patch rows of the size x size image, fused:
+// one CTA per patch row, one thread per (channel, ky, kx) element.
+__global__ void resize_patchify_kernel(const uint8_t* __restrict__ img, int H,
+                                       int W, int size, int P, float m0, float m1,
+                                       float m2, float s0, float s1, float s2,
+                                       bf16* __restrict__ out, long long ldo) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int g = size / P;
+  const int r = blockIdx.x;
+  const int v = r / (g * g), py = (r / g) % g, px = r % g;
+  const int K = 3 * P * P;
+  const uint8_t* src = img + (long long)v * H * W * 3;
+  bf16* o = out + (long long)r * ldo;
+  for (int col = threadIdx.x; col < ldo; col += blockDim.x) {
+    float val = 0.f;
+    if (col < K) {
+      const int c = col / (P * P), ky = (col / P) % P, kx = col % P;
+      const int y = py * P + ky, x = px * P + kx;
+      int x0, x1, a0, a1, y0, y1, b0, b1;
+      resize_taps(x, size, W, true, x0, x1, a0, a1);
+      resize_taps(y, size, H, false, y0, y1, b0, b1);
+      const uint8_t* r0 = src + (long long)y0 * W * 3 + c;
+      const uint8_t* r1 = src + (long long)y1 * W * 3 + c;
+      const int h0 = r0[x0 * 3] * a0 + r0[x1 * 3] * a1;
+      const int h1 = r1[x0 * 3] * a0 + r1[x1 * 3] * a1;
+      const int q = (((h0 >> 4) * b0) >> 16) + (((h1 >> 4) * b1) >> 16);
+      const int u8 = min(max((q + 2) >> 2, 0), 255);
+      const float mean = c == 0 ? m0 : (c == 1 ? m1 : m2);
+      const float sd = c == 0 ? s0 : (c == 1 ? s1 : s2);
+      val = ((float)u8 - mean) / (sd + 1e-8f);
+    }
+    o[col] = __float2bfloat16(val);
+  }
+}
+
 // uint8 HWC images -> normalised bf16 patch rows.  One CTA per patch row.
 __global__ void patchify_kernel(const uint8_t* __restrict__ img, int H, int W,
                                 int P, float m0, float m1, float m2, float s0,

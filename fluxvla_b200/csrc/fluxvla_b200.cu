@@ -615,6 +615,22 @@ int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
                   (long long)ldo);
 }
 
+int fvb_resize_patchify(const uint8_t* images, int32_t views,
+                        int32_t src_height, int32_t src_width, int32_t size,
+                        int32_t patch, const float* mean3, const float* std3,
+                        void* out, int64_t ldo, void* stream) {
+  if (!images || !out || !mean3 || !std3 || views <= 0 || patch <= 0 ||
+      size <= 0 || size % patch || src_height <= 0 || src_width <= 0 ||
+      ldo < 3 * patch * patch)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_resize_patchify: bad arguments");
+  const int rows = views * (size / patch) * (size / patch);
+  return launch_k("fvb_resize_patchify", fvb::resize_patchify_kernel, dim3(rows),
+                  dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), images,
+                  (int)src_height, (int)src_width, (int)size, (int)patch, mean3[0],
+                  mean3[1], mean3[2], std3[0], std3[1], std3[2], (bf16*)out,
+                  (long long)ldo);
+}
+
 int fvb_embed_tokens(const int64_t* ids, int32_t n, const void* table,
                      int32_t dim, float scale, float* out, int64_t ldo,
                      void* stream) {

@@ -73,8 +73,14 @@ class PI0EngineB200:
 
     def __init__(self, cfg: PI0Config, weights: Dict[str, torch.Tensor],
                  prefix_len: int, device='cuda', attn_splits: int = 0,
-                 loop_impl: str = 'mega'):
+                 loop_impl: str = 'mega', camera_hw: Optional[tuple] = None):
         self.cfg = cfg
+        # camera frame size (H, W) of the uint8 views handed to
+        # predict_action; frames not already image_size x image_size are
+        # resized on the device (OpenCV INTER_LINEAR, fused with normalise
+        # and the patch layout)
+        self.camera_hw = tuple(camera_hw) if camera_hw else (cfg.image_size,
+                                                            cfg.image_size)
         # 'mega': one persistent cooperative kernel per denoise step for all
         # expert layers (fvb_expert_step); 'ops': one launch per operator
         assert loop_impl in ('mega', 'ops')
@@ -177,7 +183,7 @@ class PI0EngineB200:
         if self.has_vision:
             R = cfg.n_views * cfg.tokens_per_view
             Wv = cfg.vis_width
-            B['images'] = z(cfg.n_views, cfg.image_size, cfg.image_size, 3,
+            B['images'] = z(cfg.n_views, self.camera_hw[0], self.camera_hw[1], 3,
                             dt=torch.uint8)
             B['patches'] = z(R, self.P['patch_w'].shape[1])
             B['v_res'] = z(R, Wv, dt=F32)
@@ -332,8 +338,12 @@ class PI0EngineB200:
         cfg, P, B = self.cfg, self.P, self.B
         Wv, R = cfg.vis_width, cfg.n_views * cfg.tokens_per_view
         hdv = Wv // cfg.vis_heads
-        ops.patchify(B['images'], cfg.patch, self.mean3, self.std3,
-                     B['patches'])
+        if self.camera_hw == (cfg.image_size, cfg.image_size):
+            ops.patchify(B['images'], cfg.patch, self.mean3, self.std3,
+                         B['patches'])
+        else:
+            ops.resize_patchify(B['images'], cfg.image_size, cfg.patch,
+                                self.mean3, self.std3, B['patches'])
         ops.gemm(B['patches'], P['patch_w'], B['v_res'], epilogue=EPI_F32_STORE,
                  bias=P['patch_b'], row_add=P['pos'],
                  row_add_mod=cfg.tokens_per_view)

@@ -151,6 +151,18 @@ def patchify(images_u8: torch.Tensor, patch: int, mean3, std3,
                                   _ptr(out), out.stride(0), _stream()))
 
 
+def resize_patchify(images_u8: torch.Tensor, size: int, patch: int, mean3,
+                    std3, out: torch.Tensor) -> None:
+    """uint8 [V,H,W,3] of any size -> OpenCV INTER_LINEAR resize to
+    size x size -> normalise -> bf16 patch rows (as patchify)."""
+    V, H, W, _ = images_u8.shape
+    m = (C.c_float * 3)(*[float(x) for x in mean3])
+    s = (C.c_float * 3)(*[float(x) for x in std3])
+    check(_lib.lib().fvb_resize_patchify(_ptr(images_u8), V, H, W, size, patch,
+                                         C.cast(m, C.c_void_p), C.cast(s, C.c_void_p),
+                                         _ptr(out), out.stride(0), _stream()))
+
+
 def embed_tokens(ids: torch.Tensor, table: torch.Tensor, scale: float,
                  out: torch.Tensor) -> None:
     check(_lib.lib().fvb_embed_tokens(_ptr(ids), ids.numel(), _ptr(table),

@@ -257,6 +257,20 @@ int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
                  int32_t width, int32_t patch, const float* mean3,
                  const float* std3, void* out, int64_t ldo, void* stream);
 
+/* Fused camera preprocessing: uint8 HWC views [views, src_height,
+ * src_width, 3] of any size -> resize to size x size with OpenCV's
+ * INTER_LINEAR (bit-exact uint8: the same taps and 11-bit fixed-point
+ * weights) -> (x - mean) / (std + 1e-8) -> the bf16 patch rows of
+ * fvb_patchify [views*(size/patch)^2, ldo].  mean3 / std3: HOST arrays.
+ * Replaces: ResizeImages (fluxvla/transforms/transform_images.py:80-144,
+ * cv2.resize INTER_LINEAR), NormalizeImages (:313) and the im2col half of
+ * conv2d_embed_res (fluxvla/ops/atomic_ops.py:36); the reference runs the
+ * first two on the host per request.                                      */
+int fvb_resize_patchify(const uint8_t* images, int32_t views,
+                        int32_t src_height, int32_t src_width, int32_t size,
+                        int32_t patch, const float* mean3, const float* std3,
+                        void* out, int64_t ldo, void* stream);
+
 /* out_f32[i, :] = table_bf16[ids[i], :] * scale.
  * Replaces: embed_tokens(...) * sqrt(width)
  * (fluxvla/models/vlas/pi0_flowmatching.py:233-237).                      */

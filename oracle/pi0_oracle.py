@@ -235,6 +235,48 @@ def gemma_model(x: Tensor, W: Dict[str, Tensor], p: str, n_layers: int,
 # SigLIP vision tower (HF SiglipVisionModel, vision_use_head=False)
 # ---------------------------------------------------------------------------
 
+def _resize_taps(dst: int, src: int, clamp_weights: bool):
+    """Source taps and 11-bit fixed-point weights of one axis of OpenCV's
+    INTER_LINEAR resize (the `cv2.resize` that ResizeImages calls,
+    fluxvla/transforms/transform_images.py:103-106): f = (d+0.5)*scale-0.5
+    with scale = 1/(dst/src) in float64, rounded to float32, s = floor(f), weights round((1-f')*2048), round(f'*2048)
+    (half to even).  Along x a tap left of 0 or at/after the last column is
+    clamped with its fraction set to 0; along y the fraction is kept and only
+    the row indices are clamped."""
+    import numpy as np
+    d = np.arange(dst, dtype=np.float64)
+    scale = 1.0 / (dst / src)  # OpenCV: 1 / (dst / src) in double
+    f = ((d + 0.5) * scale - 0.5).astype(np.float32)
+    s = np.floor(f).astype(np.int64)
+    f = (f - s.astype(np.float32)).astype(np.float32)
+    if clamp_weights:
+        f[s < 0] = 0
+        s[s < 0] = 0
+        f[s >= src - 1] = 0
+        s[s >= src - 1] = src - 1
+    w0 = np.rint((np.float32(1.0) - f) * np.float32(2048)).astype(np.int64)
+    w1 = np.rint(f * np.float32(2048)).astype(np.int64)
+    return np.clip(s, 0, src - 1), np.clip(s + 1, 0, src - 1), w0, w1
+
+
+def resize_linear_u8(img_hwc, height: int, width: int):
+    """uint8 [H, W, C] -> uint8 [height, width, C] exactly as OpenCV's
+    INTER_LINEAR: horizontal pass in int (S[x0]*a0 + S[x1]*a1), vertical
+    pass in the fixed-point form of its vectorised kernel,
+    (((r0>>4)*b0 >> 16) + ((r1>>4)*b1 >> 16) + 2) >> 2, saturated to
+    [0, 255].  Pinned against cv2.resize by tests/golden (make_resize_golden)."""
+    import numpy as np
+    img = np.asarray(img_hwc)
+    h, w = img.shape[:2]
+    x0, x1, a0, a1 = _resize_taps(width, w, True)
+    y0, y1, b0, b1 = _resize_taps(height, h, False)
+    rows = (img[:, x0].astype(np.int64) * a0[None, :, None] +
+            img[:, x1].astype(np.int64) * a1[None, :, None])
+    v = (((rows[y0] >> 4) * b0[:, None, None]) >> 16) + \
+        (((rows[y1] >> 4) * b1[:, None, None]) >> 16)
+    return np.clip((v + 2) >> 2, 0, 255).astype(np.uint8)
+
+
 def normalize_images(images_u8: Tensor, means, stds) -> Tensor:
     """NormalizeImages, fluxvla/transforms/transform_images.py:313-372:
     (x - mean) / (std + 1e-8) per channel.  Input uint8 HWC [V,H,W,3];

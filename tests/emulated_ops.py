@@ -153,6 +153,13 @@ def patchify(img, patch, mean3, std3, out):
     out[:, :p.shape[1]] = p.to(out.dtype)
 
 
+def resize_patchify(img, size, patch, mean3, std3, out):
+    from oracle.pi0_oracle import resize_linear_u8
+    r = torch.stack([torch.from_numpy(resize_linear_u8(v.numpy(), size, size))
+                     for v in img.cpu()])
+    patchify(r, patch, mean3, std3, out)
+
+
 def embed_tokens(ids, table, scale, out):
     _count[0] += 1
     out.copy_(table[ids.long()].float() * scale)
@@ -238,7 +245,8 @@ def install(monkeypatch):
     for name in ['gemm', 'attn_args', 'attention', 'attention_workspace_bytes',
                  'gemm_workspace_bytes', 'expert_args', 'expert_step',
                  'expert_workspace_bytes',
-                 'norm', 'patchify', 'embed_tokens', 'small_linear',
+                 'norm', 'patchify', 'resize_patchify', 'embed_tokens',
+                 'small_linear',
                  'launch_count']:
         monkeypatch.setattr(ops, name, globals()[name])
     monkeypatch.setattr(engine.torch.cuda, 'synchronize', lambda *a: None)

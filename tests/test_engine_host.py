@@ -64,3 +64,28 @@ def test_step_times_and_sinusoid_match_oracle():
     assert dt == float(torch.tensor(-0.1, dtype=torch.float32))
     torch.testing.assert_close(sinusoid(ts, 64),
                                O.sinusoidal_time(torch.tensor(ts), 64))
+
+
+def test_engine_resizes_camera_frames(monkeypatch):
+    """Frames of another size go through the device resize (OpenCV
+    INTER_LINEAR) and give the actions of the pre-resized frames."""
+    import numpy as np
+    emulated_ops.install(monkeypatch)
+    cfg = _tiny(False)
+    W = make_weights(cfg, 9)
+    g = torch.Generator().manual_seed(11)
+    n_tok = 5
+    cam = torch.randint(0, 256, (cfg.n_views, 40, 33, 3), generator=g,
+                        dtype=torch.uint8)
+    toks = torch.randint(0, cfg.vocab, (1, n_tok), generator=g)
+    state = torch.randn(1, cfg.state_dim, generator=g)
+    noise = torch.randn(1, cfg.n_actions, cfg.action_dim, generator=g)
+    E = cfg.n_views * cfg.tokens_per_view + n_tok
+    eng = PI0EngineB200(cfg, W, prefix_len=E, device='cpu', camera_hw=(40, 33))
+    eng.load_inputs(cam, toks, None, None, state, noise)
+    eng.run()
+    out = eng.actions[None]
+    small = torch.stack([torch.from_numpy(O.resize_linear_u8(v.numpy(), 28, 28))
+                         for v in cam])
+    ref = O.predict_action(cfg, W, small, toks, state, noise)
+    torch.testing.assert_close(out, ref, atol=2e-2, rtol=1e-2)

@@ -460,6 +460,33 @@ def test_small_linear_paths(T, K, N, mode, act, xoff):
         torch.testing.assert_close(out, ref, atol=1e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize('h,w,size,patch', [(256, 256, 224, 14), (480, 640, 224, 14),
+                                            (20, 30, 28, 14), (61, 47, 56, 14),
+                                            (224, 224, 224, 14), (96, 96, 48, 12)])
+def test_resize_patchify_bit_exact(h, w, size, patch):
+    """Device resize (OpenCV INTER_LINEAR) + normalise + patch rows equal the
+    oracle's restatement bit for bit (uint8 resize, then the same f32
+    normalise and bf16 rounding)."""
+    import numpy as np
+    from oracle.pi0_oracle import resize_linear_u8
+    V = 3
+    mean3, std3 = (0.485 * 255, 0.456 * 255, 0.406 * 255), (0.229 * 255, 0.224 * 255, 0.225 * 255)
+    rng = np.random.default_rng(h * w)
+    imgs = rng.integers(0, 256, (V, h, w, 3), dtype=np.uint8)
+    g = size // patch
+    K = 3 * patch * patch
+    out = torch.full((V * g * g, K + 4), 9.0, device=DEV, dtype=torch.bfloat16)
+    ops.resize_patchify(torch.from_numpy(imgs).to(DEV), size, patch, mean3, std3, out)
+    r = torch.from_numpy(np.stack([resize_linear_u8(v, size, size) for v in imgs]))
+    x = r.float().permute(0, 3, 1, 2)
+    x = (x - torch.tensor(mean3)[:, None, None]) / (torch.tensor(std3)[:, None, None] + 1e-8)
+    p = x.unfold(2, patch, patch).unfold(3, patch, patch)
+    ref = p.permute(0, 2, 3, 1, 4, 5).reshape(V * g * g, K).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.equal(out[:, :K].cpu(), ref)
+    assert (out[:, K:].float() == 0).all()
+
+
 @pytest.mark.parametrize('split', [0, 3, 16])
 def test_gemm_swap_split_fixup(split):
     """Swapped split-K GEMMs with non-additive epilogues reduce their splits

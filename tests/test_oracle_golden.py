@@ -63,3 +63,15 @@ def test_gemma_layer_cfg0_geometry_matches_reference():
     W = make_weights(cfg, d['seed'], parts=('llm',))
     out = O.gemma_layer_causal(cfg, W, d['x'])
     torch.testing.assert_close(out, d['out'], atol=1e-4, rtol=1e-4)
+
+
+def test_resize_matches_opencv_golden():
+    """The oracle's INTER_LINEAR restatement against cv2.resize outputs
+    (tests/golden/make_resize_golden.py): bit-exact uint8."""
+    import os
+    from tests.golden.make_resize_golden import source
+    d = torch.load(os.path.join(os.path.dirname(__file__), 'golden', 'resize_u8.pt'))
+    from oracle.pi0_oracle import resize_linear_u8
+    for (seed, h, w, H, W) in d['cases']:
+        got = resize_linear_u8(source(seed, h, w), H, W)
+        assert torch.equal(torch.from_numpy(got), d['outputs'][(seed, h, w, H, W)]), (h, w, H, W)
