@@ -12,6 +12,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, 'libfluxvla_b200.so')
 
 FVB_OK = 0
+(FVB_ERR_INVALID_ARG, FVB_ERR_UNSUPPORTED, FVB_ERR_CUDA, FVB_ERR_DEVICE_TIMEOUT,
+ FVB_ERR_WORKSPACE) = range(1, 6)
 EPI_BF16, EPI_F32_STORE, EPI_F32_ACC, EPI_GEGLU, EPI_QKV_ROPE = range(5)
 ACT_NONE, ACT_GELU_TANH, ACT_SILU = range(3)
 NORM_GEMMA_RMS, NORM_ADA_RMS, NORM_LAYER = range(3)
@@ -88,6 +90,7 @@ EXPORTS = {
                                       C.c_int32, C.c_int32, C.c_int32,
                                       C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_int64, C.c_void_p]),
+    'fvb_probe_wait_timeout': (C.c_int, [C.c_int64, C.c_void_p, C.c_void_p]),
     'fvb_patchify': (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                C.c_int32, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_int64, C.c_void_p]),

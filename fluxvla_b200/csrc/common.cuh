@@ -103,19 +103,24 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// records a device error) if it does not complete within FVB_WAIT_LIMIT_NS.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// records a device error) if it does not complete within limit_ns.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity,
+                                                uint64_t limit_ns) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     for (int i = 0; i < 8; ++i)
       if (mbar_try_wait_sleep(addr, parity, 20000)) return true;
-    if (globaltimer_ns() - t0 > FVB_WAIT_LIMIT_NS) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_device_error(FVB_ERR_DEVICE_TIMEOUT);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_limit(bar, parity, FVB_WAIT_LIMIT_NS);
 }
 
 // ---------------------------------------------------------------------------

@@ -355,4 +355,18 @@ __global__ void __launch_bounds__(256)
     small_linear_store(out, ldo, t, n, mode, alpha, small_linear_finish(acc, bias, n, act));
 }
 
+// Failure-path probe: one thread waits on an mbarrier that nothing arrives
+// on, through the same bounded wait as every kernel here, with a short
+// limit; the wait gives up, records FVB_ERR_DEVICE_TIMEOUT in the status
+// word and the kernel returns normally (the context stays usable).
+__device__ int g_probe_result;
+__global__ void wait_timeout_probe_kernel(unsigned long long limit_ns, int* gave_up) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const bool ok = mbar_wait_limit(&bar, 0, limit_ns);
+  *gave_up = ok ? 0 : 1;
+}
+
 }  // namespace fvb

@@ -257,6 +257,23 @@ int fvb_get_device_status(int* status, int reset) {
   return FVB_OK;
 }
 
+int fvb_probe_wait_timeout(int64_t limit_ns, int* gave_up_host, void* stream) {
+  if (!gave_up_host) return fail(FVB_ERR_INVALID_ARG, "gave_up_host is NULL");
+  if (limit_ns < 1000000) limit_ns = 1000000;
+  if (limit_ns > (int64_t)FVB_WAIT_LIMIT_NS) limit_ns = (int64_t)FVB_WAIT_LIMIT_NS;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int* d = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&d), fvb::g_probe_result) != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "probe: symbol lookup failed");
+  fvb::wait_timeout_probe_kernel<<<1, 32, 0, st>>>((unsigned long long)limit_ns, d);
+  int r = check_launch("fvb_probe_wait_timeout");
+  if (!r && cudaMemcpyAsync(gave_up_host, d, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    r = fail(FVB_ERR_CUDA, "probe: copy failed");
+  if (!r && cudaStreamSynchronize(st) != cudaSuccess)
+    r = fail(FVB_ERR_CUDA, "probe: %s", cudaGetErrorString(cudaGetLastError()));
+  return r;
+}
+
 int fvb_gemm_trace_next(void) {
   g_trace_next = 1;
   return FVB_OK;

@@ -182,6 +182,13 @@ def small_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *,
                                       out.stride(0), _stream()))
 
 
+def probe_wait_timeout(limit_s: float = 0.05) -> bool:
+    """Run the bounded-wait failure probe; True if the wait gave up."""
+    g = C.c_int(0)
+    check(_lib.lib().fvb_probe_wait_timeout(int(limit_s * 1e9), C.byref(g), _stream()))
+    return g.value == 1
+
+
 def device_status(reset: bool = False) -> int:
     s = C.c_int(0)
     check(_lib.lib().fvb_get_device_status(C.byref(s), int(reset)))

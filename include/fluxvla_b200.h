@@ -304,6 +304,13 @@ int fvb_expert_trace_read(uint64_t* host_out, int32_t max_ctas);
 
 /* Status and diagnostics. */
 int fvb_get_device_status(int* status, int reset);
+
+/* Failure-path self test (no reference counterpart): launches one thread
+ * that waits, through the library's bounded mbarrier wait, on a barrier
+ * nothing arrives on, with limit_ns (clamped to [1 ms, 2 s]).  The wait
+ * gives up, sets FVB_ERR_DEVICE_TIMEOUT in the device status word and the
+ * kernel returns; *gave_up_host = 1.  The call synchronises the stream.   */
+int fvb_probe_wait_timeout(int64_t limit_ns, int* gave_up_host, void* stream);
 const char* fvb_last_error(void);
 int fvb_version(void);
 /* Number of kernels this library has launched since load (host counter). */

@@ -540,3 +540,20 @@ def test_gemm_split_without_workspace_is_rejected():
     out = torch.empty(51, 1024, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match='workspace'):
         ops.gemm(w, x, out, swap=True, split_k=4)
+
+
+def test_bounded_wait_gives_up_and_context_stays_usable():
+    """Failure path without a GPU fault: a wait on an mbarrier that nothing
+    arrives on runs out after its (short) limit, the kernel records
+    FVB_ERR_DEVICE_TIMEOUT and returns, and the next kernels run normally."""
+    from fluxvla_b200._lib import FVB_ERR_DEVICE_TIMEOUT
+    ops.device_status(reset=True)
+    assert ops.probe_wait_timeout(0.05)
+    assert ops.device_status(reset=True) == FVB_ERR_DEVICE_TIMEOUT
+    assert ops.device_status() == 0
+    a, b = rnd(64, 64), rnd(64, 64)
+    out = torch.empty(64, 64, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(a, b, out)
+    torch.cuda.synchronize()
+    close(out, a.float() @ b.float().t())
+    assert ops.device_status() == 0
