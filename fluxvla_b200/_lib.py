@@ -36,7 +36,7 @@ class GemmArgs(C.Structure):
                 ('norm_mode', C.c_int32), ('norm_out', C.c_void_p),
                 ('ld_norm_out', C.c_int64), ('norm_w', C.c_void_p),
                 ('norm_b', C.c_void_p), ('norm_eps', C.c_float),
-                ('norm_sync', C.c_void_p)]
+                ('norm_sync', C.c_void_p), ('pair', C.c_int32)]
 
 
 class AttnArgs(C.Structure):

@@ -13,6 +13,7 @@
 #include "elementwise.cuh"
 #include "expert_mega.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_pair.cuh"
 
 namespace {
 
@@ -173,6 +174,74 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
   const int grid = d.n_work < sm_count() ? d.n_work : sm_count();
   return launch_k("fvb_gemm", kern, dim3(grid), dim3(fvb::GEMM_THREADS),
                   (size_t)C::SMEM, st, ma, mb, mo, d);
+}
+
+template <int BN, int EPI>
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb,
+                     const fvb::GemmDev& d, cudaStream_t st) {
+  using C = fvb::pair::PairCfg<BN>;
+  auto kern = fvb::pair::gemm_pair_kernel<BN, EPI>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM) != cudaSuccess)
+      return fail(FVB_ERR_CUDA, "gemm pair smem attribute: %s",
+                  cudaGetErrorString(cudaGetLastError()));
+    attr = true;
+  }
+  const int pairs_max = sm_count() / 2;
+  const int pairs = d.n_work < pairs_max ? d.n_work : pairs_max;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(fvb::pair::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, d);
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "fvb_gemm (pair): launch failed: %s", cudaGetErrorString(e));
+  return check_launch("fvb_gemm (pair)");
+}
+
+int gemm_pair(const fvb_gemm_args* a, void* stream) {
+  constexpr int BN = 208;
+  if (!a->swap || (a->epilogue != FVB_EPI_GEGLU && a->epilogue != FVB_EPI_F32_ACC) ||
+      (a->block_n != 0 && a->block_n != BN) || a->norm_out || a->row_add)
+    return fail(FVB_ERR_UNSUPPORTED,
+                "fvb_gemm: pair tiles need swap, GEGLU or F32_ACC, block_n 208");
+  if (a->epilogue == FVB_EPI_GEGLU && (a->m % 2 || a->ldo % 1))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: GEGLU needs an even feature count");
+  const int k_tiles = (a->k + fvb::GEMM_BK - 1) / fvb::GEMM_BK;
+  int split = a->split_k > 0 ? a->split_k : 1;
+  if (split > k_tiles) split = k_tiles;
+  const int kt_per = (k_tiles + split - 1) / split;
+  split = (k_tiles + kt_per - 1) / kt_per;
+  if (split > 1 && a->epilogue != FVB_EPI_F32_ACC)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: pair split-K needs FVB_EPI_F32_ACC");
+  CUtensorMap ma, mb;
+  int r = make_map(&ma, a->a, a->m, a->k, a->lda, 128);
+  if (!r) r = make_map(&mb, a->b, a->n, a->k, a->ldb, BN / 2);
+  if (r) return r;
+  fvb::GemmDev d;
+  memset(&d, 0, sizeof(d));
+  d.m = a->m; d.n = a->n; d.k = a->k;
+  d.k_tiles = k_tiles; d.kt_per_split = kt_per; d.split = split;
+  d.out = a->out; d.ldo = a->ldo;
+  d.bias = a->bias; d.gate = a->gate; d.alpha = a->alpha;
+  d.m_tiles = (a->m + 255) / 256;
+  d.n_tiles = (a->n + BN - 1) / BN;
+  d.n_work = d.m_tiles * d.n_tiles * d.split;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (a->epilogue == FVB_EPI_GEGLU) return launch_gemm_pair<BN, FVB_EPI_GEGLU>(ma, mb, d, st);
+  return launch_gemm_pair<BN, FVB_EPI_F32_ACC>(ma, mb, d, st);
 }
 
 int g_trace_next = 0;
@@ -340,6 +409,8 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: GEGLU output must be 16B aligned");
   if (a->row_add && a->row_add_mod <= 0)
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: row_add_mod must be > 0");
+
+  if (a->pair) return gemm_pair(a, stream);
 
   int bn = a->block_n;
   if (bn == 0) bn = a->swap ? 64 : 128;

@@ -48,7 +48,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
          head_dim: int = 0, rope_cs: Optional[torch.Tensor] = None,
          positions: Optional[torch.Tensor] = None,
          workspace: Optional[torch.Tensor] = None,
-         norm: Optional[tuple] = None) -> None:
+         norm: Optional[tuple] = None, pair: bool = False) -> None:
     """C[M,N] = A[M,K] @ B[N,K]^T with a fused epilogue (see fvb_gemm).
     split_k=0 picks the split automatically for swapped GEMMs; a swapped
     split GEMM with a non-additive epilogue needs ``workspace`` (a zeroed
@@ -76,7 +76,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
                     n_heads=n_heads, head_dim=head_dim, rope_cs=_ptr(rope_cs),
                     positions=_ptr(positions), workspace=_ptr(workspace),
                     workspace_bytes=0 if workspace is None else
-                    workspace.numel() * workspace.element_size())
+                    workspace.numel() * workspace.element_size(),
+                    pair=int(pair))
     if norm is not None:
         mode, nout, nw, nb, eps, sync = norm
         args.norm_mode = mode

@@ -108,6 +108,11 @@ typedef struct fvb_gemm_args {
   const void* norm_b;
   float norm_eps;
   void* norm_sync;
+  /* pair = 1: two-SM tiles (a 2-CTA cluster, tcgen05.mma.cta_group::2):
+   * 256 weight rows x block_n tokens per pair, each SM loading half of the
+   * token operand.  Swapped orientation only (a = weights), epilogues
+   * FVB_EPI_GEGLU and FVB_EPI_F32_ACC, block_n 0 (= 208) or 208.          */
+  int32_t pair;
 } fvb_gemm_args;
 
 /* tcgen05/TMEM tensor-core GEMM with fused epilogues.

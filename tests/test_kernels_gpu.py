@@ -557,3 +557,29 @@ def test_bounded_wait_gives_up_and_context_stays_usable():
     torch.cuda.synchronize()
     close(out, a.float() @ b.float().t())
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize('F,T,K,epi,split', [
+    (1024, 816, 512, EPI_GEGLU, 1),
+    (640, 100, 256, EPI_GEGLU, 1),
+    (512, 816, 1024, EPI_F32_ACC, 1),
+    (384, 300, 2048, EPI_F32_ACC, 3)])
+def test_gemm_pair_two_sm(F, T, K, epi, split):
+    """Two-SM (cta_group::2) swapped GEMM: 256 weight rows x 208 tokens per
+    CTA pair, each SM loading half of the token tile."""
+    torch.manual_seed(F + T)
+    w, x = rnd(F, K, std=0.02), rnd(T, K)
+    acc = x.float() @ w.float().t()
+    if epi == EPI_GEGLU:
+        out = torch.empty(T, F // 2, device=DEV, dtype=torch.bfloat16)
+        ops.gemm(w, x, out, epilogue=EPI_GEGLU, swap=True, pair=True)
+        ref = torch.nn.functional.gelu(acc[:, 0::2], approximate='tanh') * acc[:, 1::2]
+        torch.cuda.synchronize()
+        close(out, ref)
+    else:
+        res = torch.randn(T, F, device=DEV)
+        out = res.clone()
+        ops.gemm(w, x, out, epilogue=EPI_F32_ACC, swap=True, pair=True, split_k=split)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out, res + acc, atol=2e-3, rtol=2e-3)
+    assert ops.device_status() == 0
