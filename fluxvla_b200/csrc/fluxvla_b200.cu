@@ -105,6 +105,27 @@ int make_out_map(CUtensorMap* m, void* ptr, bool f32, int64_t rows,
   return FVB_OK;
 }
 
+// Output tensor map with a dense (unswizzled) box of box_rows x box_cols.
+int make_out_map_dense(CUtensorMap* m, void* ptr, bool f32, int64_t rows,
+                       int64_t cols, int64_t ld, int box_cols, int box_rows) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return fail(FVB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int eb = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * eb)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   2, ptr, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FVB_ERR_INVALID_ARG, "output tensor map encode failed (%d)", (int)r);
+  return FVB_OK;
+}
+
 // TMA-store epilogues are on unless FVB_TMA_OUT=0.
 bool tma_out_enabled() {
   static const int v = [] {
@@ -176,9 +197,11 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
                   (size_t)C::SMEM, st, ma, mb, mo, d);
 }
 
+int g_trace_next = 0;
+
 template <int BN, int EPI>
 int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb,
-                     const fvb::GemmDev& d, cudaStream_t st) {
+                     const CUtensorMap& mo, const fvb::GemmDev& d, cudaStream_t st) {
   using C = fvb::pair::PairCfg<BN>;
   auto kern = fvb::pair::gemm_pair_kernel<BN, EPI>;
   static bool attr = false;
@@ -205,7 +228,7 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb,
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, d);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, d);
   if (e != cudaSuccess)
     return fail(FVB_ERR_CUDA, "fvb_gemm (pair): launch failed: %s", cudaGetErrorString(e));
   return check_launch("fvb_gemm (pair)");
@@ -226,9 +249,15 @@ int gemm_pair(const fvb_gemm_args* a, void* stream) {
   split = (k_tiles + kt_per - 1) / kt_per;
   if (split > 1 && a->epilogue != FVB_EPI_F32_ACC)
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: pair split-K needs FVB_EPI_F32_ACC");
-  CUtensorMap ma, mb;
+  const bool geglu = a->epilogue == FVB_EPI_GEGLU;
+  if ((reinterpret_cast<uintptr_t>(a->out) & 15) || (a->ldo * (geglu ? 2 : 4)) % 16)
+    return fail(FVB_ERR_INVALID_ARG,
+                "fvb_gemm: pair tiles need a 16-byte aligned output and row stride");
+  CUtensorMap ma, mb, mo;
   int r = make_map(&ma, a->a, a->m, a->k, a->lda, 128);
   if (!r) r = make_map(&mb, a->b, a->n, a->k, a->ldb, BN / 2);
+  if (!r) r = make_out_map_dense(&mo, a->out, !geglu, a->n, geglu ? a->m / 2 : a->m,
+                                 a->ldo, geglu ? 16 : 32, 16);
   if (r) return r;
   fvb::GemmDev d;
   memset(&d, 0, sizeof(d));
@@ -239,12 +268,13 @@ int gemm_pair(const fvb_gemm_args* a, void* stream) {
   d.m_tiles = (a->m + 255) / 256;
   d.n_tiles = (a->n + BN - 1) / BN;
   d.n_work = d.m_tiles * d.n_tiles * d.split;
+  d.trace = g_trace_next ? 1 : 0;
+  g_trace_next = 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (a->epilogue == FVB_EPI_GEGLU) return launch_gemm_pair<BN, FVB_EPI_GEGLU>(ma, mb, d, st);
-  return launch_gemm_pair<BN, FVB_EPI_F32_ACC>(ma, mb, d, st);
+  if (geglu) return launch_gemm_pair<BN, FVB_EPI_GEGLU>(ma, mb, mo, d, st);
+  return launch_gemm_pair<BN, FVB_EPI_F32_ACC>(ma, mb, mo, d, st);
 }
 
-int g_trace_next = 0;
 
 // Tensor-core attention for unsplit attention without suffix block masks
 // (the SigLIP and Gemma prefix prefills); on unless FVB_ATTN_TC=0.

@@ -385,6 +385,9 @@ class PI0EngineB200:
     # until the slowest tile is done, which costs more than the norm launch
     # whose start overlaps the GEMM's tail under programmatic dependent launch.
     fused_norm_sites = frozenset()
+    # residual GEMM call sites run as two-SM pair tiles (swapped orientation,
+    # 256 weight rows per CTA pair, fvb_gemm `pair`) with these K splits
+    pair_sites = {}
     # key splits of the Gemma prefix attention (tcgen05 kernel + combine).
     # 1: measured on the full prefill, 2 splits (102 CTAs + the combine of
     # f32 partials) cost 0.2 ms more than 51 unsplit CTAs
@@ -393,7 +396,12 @@ class PI0EngineB200:
     def _residual_gemm(self, site, a, w, res, kw, norm):
         """res += a @ w^T, then norm(res) -> bf16 (mode, out, w, b)."""
         mode, out, nw, nb = norm
-        if site in self.fused_norm_sites:
+        if site in self.pair_sites:
+            ops.gemm(w, a, res, epilogue=EPI_F32_ACC, swap=True, pair=True,
+                     split_k=self.pair_sites[site],
+                     **{k: v for k, v in kw.items() if k not in ('block_n', 'split_k')})
+            ops.norm(mode, res, out, w=nw, b=nb)
+        elif site in self.fused_norm_sites:
             ops.gemm(a, w, res, epilogue=EPI_F32_ACC,
                      norm=(mode, out, nw, nb, 1e-6, self.B['norm_sync']), **kw)
         else:
