@@ -16,7 +16,7 @@ FVB_OK = 0
  FVB_ERR_WORKSPACE) = range(1, 6)
 EPI_BF16, EPI_F32_STORE, EPI_F32_ACC, EPI_GEGLU, EPI_QKV_ROPE = range(5)
 ACT_NONE, ACT_GELU_TANH, ACT_SILU = range(3)
-NORM_GEMMA_RMS, NORM_ADA_RMS, NORM_LAYER = range(3)
+NORM_GEMMA_RMS, NORM_ADA_RMS, NORM_LAYER, NORM_RMS, NORM_ADA_STYLE = range(5)
 
 
 class GemmArgs(C.Structure):
@@ -36,7 +36,10 @@ class GemmArgs(C.Structure):
                 ('norm_mode', C.c_int32), ('norm_out', C.c_void_p),
                 ('ld_norm_out', C.c_int64), ('norm_w', C.c_void_p),
                 ('norm_b', C.c_void_p), ('norm_eps', C.c_float),
-                ('norm_sync', C.c_void_p), ('pair', C.c_int32)]
+                ('norm_sync', C.c_void_p), ('pair', C.c_int32),
+                ('res', C.c_void_p), ('ld_res', C.c_int64),
+                ('gate_tok', C.c_void_p), ('ld_gate_tok', C.c_int64),
+                ('rope_interleaved', C.c_int32)]
 
 
 class AttnArgs(C.Structure):
@@ -82,6 +85,10 @@ EXPORTS = {
     'fvb_attention': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),
     'fvb_attention_workspace_bytes': (C.c_int64, [C.POINTER(AttnArgs)]),
     'fvb_attention_combine': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),
+    'fvb_norm_bf16': (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_void_p,
+                                C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
+                                C.c_float, C.c_void_p]),
     'fvb_norm': (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_void_p,
                            C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,

@@ -369,4 +369,82 @@ __global__ void wait_timeout_probe_kernel(unsigned long long limit_ns, int* gave
   *gave_up = ok ? 0 : 1;
 }
 
+
+// ---------------------------------------------------------------------------
+// Norms of bf16 rows (fvb_norm_bf16): one warp per row, 8 values per lane
+// per step (16-byte loads); LayerNorm takes a second pass for the centred
+// variance as the reference kernel does.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void unpack8(const uint4 q, float (&v)[8]) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]));
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    norm_bf16_kernel(int mode, const bf16* __restrict__ x, long long ld_in,
+                     bf16* __restrict__ out, long long ld_out, int rows, int dim,
+                     const bf16* __restrict__ w, const bf16* __restrict__ b,
+                     const bf16* __restrict__ style, bf16* __restrict__ gate_out,
+                     long long ld_gate, float eps) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bf16* xr = x + (long long)row * ld_in;
+  float s = 0.f, ss = 0.f;
+  for (int c = lane * 8; c < dim; c += 256) {
+    float v[8];
+    unpack8(*reinterpret_cast<const uint4*>(xr + c), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { s += v[e]; ss += v[e] * v[e]; }
+  }
+  s = warp_sum(s);
+  ss = warp_sum(ss);
+  float mean = 0.f, rstd;
+  if (mode == FVB_NORM_LAYER) {
+    mean = s / dim;
+    float vs = 0.f;
+    for (int c = lane * 8; c < dim; c += 256) {
+      float v[8];
+      unpack8(*reinterpret_cast<const uint4*>(xr + c), v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) vs += (v[e] - mean) * (v[e] - mean);
+    }
+    rstd = rsqrtf(warp_sum(vs) / dim + eps);
+  } else {
+    rstd = rsqrtf(ss / dim + eps);
+  }
+  bf16* orow = out + (long long)row * ld_out;
+  for (int c = lane * 8; c < dim; c += 256) {
+    float v[8], y[8];
+    unpack8(*reinterpret_cast<const uint4*>(xr + c), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = (v[e] - mean) * rstd;
+    if (mode == FVB_NORM_LAYER) {
+      float wv[8], bv[8];
+      unpack8(*reinterpret_cast<const uint4*>(w + c), wv);
+      unpack8(*reinterpret_cast<const uint4*>(b + c), bv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = y[e] * wv[e] + bv[e];
+    } else if (mode == FVB_NORM_ADA_STYLE) {
+      float sc[8], sh[8];
+      unpack8(*reinterpret_cast<const uint4*>(style + c), sc);
+      unpack8(*reinterpret_cast<const uint4*>(style + dim + c), sh);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = y[e] * (1.f + sc[e]) + sh[e];
+      *reinterpret_cast<uint4*>(gate_out + (long long)row * ld_gate + c) =
+          *reinterpret_cast<const uint4*>(style + 2 * dim + c);
+    }
+    *reinterpret_cast<uint4*>(orow + c) =
+        make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                   pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+  }
+}
+
 }  // namespace fvb

@@ -439,6 +439,17 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: GEGLU output must be 16B aligned");
   if (a->row_add && a->row_add_mod <= 0)
     return fail(FVB_ERR_INVALID_ARG, "fvb_gemm: row_add_mod must be > 0");
+  if (a->res || a->gate_tok) {
+    if (a->epilogue != FVB_EPI_BF16 || a->swap || a->pair || a->split_k > 1 ||
+        a->n % 8 || (a->res && (a->ld_res % 8 || !aligned16(a->res))) ||
+        (a->gate_tok && (a->ld_gate_tok % 8 || !aligned16(a->gate_tok))))
+      return fail(FVB_ERR_INVALID_ARG,
+                  "fvb_gemm: res / gate_tok need FVB_EPI_BF16, normal orientation, "
+                  "one K split, n and row strides multiples of 8, 16B-aligned rows");
+  }
+  if (a->rope_interleaved && (a->epilogue != FVB_EPI_QKV_ROPE || a->swap))
+    return fail(FVB_ERR_INVALID_ARG,
+                "fvb_gemm: rope_interleaved needs FVB_EPI_QKV_ROPE, normal orientation");
 
   if (a->pair) return gemm_pair(a, stream);
 
@@ -505,6 +516,9 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   d.v_out = reinterpret_cast<bf16*>(a->v_out);
   d.ld_kv = a->ld_kv; d.n_heads = a->n_heads; d.head_dim = a->head_dim;
   d.rope_cs = a->rope_cs; d.positions = a->positions;
+  d.res = reinterpret_cast<const bf16*>(a->res); d.ld_res = a->ld_res;
+  d.gate_tok = reinterpret_cast<const bf16*>(a->gate_tok); d.ld_gate_tok = a->ld_gate_tok;
+  d.rope_interleaved = a->rope_interleaved;
   d.trace = g_trace_next ? 1 : 0;
   g_trace_next = 0;
 
@@ -534,7 +548,7 @@ int fvb_gemm(const fvb_gemm_args* a, void* stream) {
   CUtensorMap mo;
   memset(&mo, 0, sizeof(mo));
   d.tma_out = 0;
-  if (!a->swap && tma_out_enabled() && aligned16(a->out)) {
+  if (!a->swap && tma_out_enabled() && aligned16(a->out) && !a->res && !a->gate_tok) {
     const int e = a->epilogue;
     const bool f32 = e == FVB_EPI_F32_ACC || (e == FVB_EPI_F32_STORE && !a->row_add);
     const bool b16 = e == FVB_EPI_BF16 || e == FVB_EPI_GEGLU;
@@ -717,6 +731,27 @@ int fvb_norm(int32_t mode, const float* x, int64_t ld_in, void* out,
                   reinterpret_cast<cudaStream_t>(stream), (int)mode, x,
                   (long long)ld_in, out, (long long)ld_out, (int)out_f32,
                   (int)dim, (const bf16*)w, (const bf16*)b, mod, eps);
+}
+
+int fvb_norm_bf16(int32_t mode, const void* x, int64_t ld_in, void* out,
+                  int64_t ld_out, int32_t rows, int32_t dim, const void* w,
+                  const void* b, const void* style, void* gate_out,
+                  int64_t ld_gate, float eps, void* stream) {
+  if (!x || !out || rows <= 0 || dim <= 0 || dim % 8 || ld_in % 8 || ld_out % 8 ||
+      !aligned16(x) || !aligned16(out))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm_bf16: bad arguments");
+  if (mode == FVB_NORM_LAYER && (!w || !b || !aligned16(w) || !aligned16(b)))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm_bf16: weight and bias required");
+  if (mode == FVB_NORM_ADA_STYLE &&
+      (!style || !gate_out || !aligned16(style) || !aligned16(gate_out) || ld_gate % 8))
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm_bf16: style and gate output required");
+  if (mode != FVB_NORM_RMS && mode != FVB_NORM_LAYER && mode != FVB_NORM_ADA_STYLE)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_norm_bf16: bad mode");
+  return launch_k("fvb_norm_bf16", fvb::norm_bf16_kernel, dim3((rows + 7) / 8), dim3(256),
+                  0, reinterpret_cast<cudaStream_t>(stream), (int)mode, (const bf16*)x,
+                  (long long)ld_in, (bf16*)out, (long long)ld_out, (int)rows, (int)dim,
+                  (const bf16*)w, (const bf16*)b, (const bf16*)style, (bf16*)gate_out,
+                  (long long)ld_gate, eps);
 }
 
 int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,

@@ -68,6 +68,12 @@ struct GemmDev {
   float norm_eps;
   int norm_mode;
   unsigned long long* norm_sync;
+  // bf16 epilogue: per-element residual and gate (bf16 [m, ld]) or null
+  const bf16* res;
+  long long ld_res;
+  const bf16* gate_tok;
+  long long ld_gate_tok;
+  int rope_interleaved;  // QKV: store rotary pairs adjacent
 };
 
 // Arrivals of one launch at the fused-norm grid barrier add up to exactly
@@ -382,10 +388,37 @@ __device__ __forceinline__ void epilogue_normal(const GemmDev& p, const EpiPre& 
       load_rope32<BN, EPI>(p, e.pos, f0 + 32, cs_next);
 
     if (EPI == FVB_EPI_BF16) {
+      if (p.res || p.gate_tok) {
+        // this row's residual / gate values of the 32 columns (n % 8 == 0)
+        uint4 rq[4], gq[4];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2)
-        srow[j >> 1] = pack_bf16x2(apply_act<ACT>(p.alpha * v[j] + colv[c + j]),
-                                   apply_act<ACT>(p.alpha * v[j + 1] + colv[c + j + 1]));
+        for (int q = 0; q < 4; ++q) {
+          const bool in = row_ok && f0 + 8 * q < n_feat;
+          rq[q] = (in && p.res)
+                      ? *reinterpret_cast<const uint4*>(p.res + (long long)t * p.ld_res + f0 + 8 * q)
+                      : make_uint4(0u, 0u, 0u, 0u);
+          gq[q] = (in && p.gate_tok)
+                      ? *reinterpret_cast<const uint4*>(p.gate_tok + (long long)t * p.ld_gate_tok +
+                                                        f0 + 8 * q)
+                      : make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);
+        }
+        const bf16* rb = reinterpret_cast<const bf16*>(rq);
+        const bf16* gb = reinterpret_cast<const bf16*>(gq);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float y0 = apply_act<ACT>(p.alpha * v[j] + colv[c + j]) * __bfloat162float(gb[j]) +
+                           __bfloat162float(rb[j]);
+          const float y1 =
+              apply_act<ACT>(p.alpha * v[j + 1] + colv[c + j + 1]) * __bfloat162float(gb[j + 1]) +
+              __bfloat162float(rb[j + 1]);
+          srow[j >> 1] = pack_bf16x2(y0, y1);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+          srow[j >> 1] = pack_bf16x2(apply_act<ACT>(p.alpha * v[j] + colv[c + j]),
+                                     apply_act<ACT>(p.alpha * v[j + 1] + colv[c + j + 1]));
+      }
       __syncwarp();
       bf16* base = reinterpret_cast<bf16*>(p.out) + (long long)t_base * p.ldo + f0;
       if ((p.ldo % 8) == 0 && (ncol % 8) == 0) {
@@ -460,7 +493,29 @@ __device__ __forceinline__ void epilogue_normal(const GemmDev& p, const EpiPre& 
         }
       }
     } else {  // FVB_EPI_QKV_ROPE: n_feat, head_dim multiples of 32
-      if (f0 < qk_end) {
+      if (f0 < qk_end && p.rope_interleaved) {
+        // rotary pairs stay adjacent: packed column order is the output order
+        const int hh = f0 / hd;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float cc = cs[2 * i], sn = cs[2 * i + 1];
+          const float a0 = v[2 * i], b0 = v[2 * i + 1];
+          srow[i] = pack_bf16x2(a0 * cc - b0 * sn, b0 * cc + a0 * sn);
+        }
+        __syncwarp();
+        bf16* base;
+        long long ld;
+        if (hh < p.n_heads) {
+          base = reinterpret_cast<bf16*>(p.out) + (long long)t_base * p.ldo + hh * hd + (f0 % hd);
+          ld = p.ldo;
+        } else {
+          base = p.k_out + (long long)t_base * p.ld_kv + (f0 % hd);
+          ld = p.ld_kv;
+        }
+        warp_writeback<16, 0>(stage, lane, rows_valid, 16, [&](int row) {
+          return reinterpret_cast<uint32_t*>(base + (long long)row * ld);
+        });
+      } else if (f0 < qk_end) {
         const int hh = f0 / hd;
         const int i0 = (f0 % hd) >> 1;
 #pragma unroll

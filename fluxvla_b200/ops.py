@@ -48,14 +48,20 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
          head_dim: int = 0, rope_cs: Optional[torch.Tensor] = None,
          positions: Optional[torch.Tensor] = None,
          workspace: Optional[torch.Tensor] = None,
-         norm: Optional[tuple] = None, pair: bool = False) -> None:
+         norm: Optional[tuple] = None, pair: bool = False,
+         res: Optional[torch.Tensor] = None,
+         gate_tok: Optional[torch.Tensor] = None,
+         rope_interleaved: bool = False) -> None:
     """C[M,N] = A[M,K] @ B[N,K]^T with a fused epilogue (see fvb_gemm).
     split_k=0 picks the split automatically for swapped GEMMs; a swapped
     split GEMM with a non-additive epilogue needs ``workspace`` (a zeroed
     uint8 tensor of gemm_workspace_bytes(...), left zeroed by the call).
     ``norm=(mode, out_bf16, w, b, eps, sync)`` normalises the finished f32
     output rows into ``out_bf16`` in the same launch (``sync``: an int64
-    device tensor, zero before first use)."""
+    device tensor, zero before first use).  ``res`` / ``gate_tok`` (bf16
+    [m, n] row-major views) make the bf16 epilogue out = res + gate_tok *
+    act(alpha*acc + bias); ``rope_interleaved`` stores rotated q / k with each
+    rotary pair adjacent."""
     lda = _rowmajor(a, 'a', BF16)
     ldb = _rowmajor(b, 'b', BF16)
     if a.shape[1] != b.shape[1]:
@@ -77,7 +83,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
                     positions=_ptr(positions), workspace=_ptr(workspace),
                     workspace_bytes=0 if workspace is None else
                     workspace.numel() * workspace.element_size(),
-                    pair=int(pair))
+                    pair=int(pair), res=_ptr(res),
+                    ld_res=0 if res is None else _rowmajor(res, 'res', BF16),
+                    gate_tok=_ptr(gate_tok),
+                    ld_gate_tok=0 if gate_tok is None else
+                    _rowmajor(gate_tok, 'gate_tok', BF16),
+                    rope_interleaved=int(rope_interleaved))
     if norm is not None:
         mode, nout, nw, nb, eps, sync = norm
         args.norm_mode = mode
@@ -128,6 +139,21 @@ def attention(args: AttnArgs) -> None:
     check(L.fvb_attention(C.byref(args), _stream()))
     if args.kv_splits > 1:
         check(L.fvb_attention_combine(C.byref(args), _stream()))
+
+
+def norm_bf16(mode: int, x: torch.Tensor, out: torch.Tensor, *, w=None,
+              b=None, style=None, gate_out=None, eps: float = 1e-6) -> None:
+    """Norm of bf16 rows (fvb_norm_bf16): NORM_RMS (no weight), NORM_LAYER
+    (w, b bf16) or NORM_ADA_STYLE (style bf16 row: scale | shift | gate;
+    the gate goes to gate_out for every row)."""
+    ld_in = _rowmajor(x, 'x', BF16)
+    ld_out = _rowmajor(out, 'out', BF16)
+    rows, dim = x.shape
+    check(_lib.lib().fvb_norm_bf16(
+        mode, _ptr(x), ld_in, _ptr(out), ld_out, rows, dim, _ptr(w), _ptr(b),
+        _ptr(style), _ptr(gate_out),
+        0 if gate_out is None else _rowmajor(gate_out, 'gate_out', BF16),
+        eps, _stream()))
 
 
 def norm(mode: int, x: torch.Tensor, out: torch.Tensor, *, w=None, b=None,

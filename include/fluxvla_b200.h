@@ -47,6 +47,8 @@ extern "C" {
 #define FVB_NORM_GEMMA_RMS 0 /* x*rsqrt(mean(x^2)+eps)*(1+w)               */
 #define FVB_NORM_ADA_RMS 1   /* x*rsqrt(mean(x^2)+eps)*(1+scale)+shift     */
 #define FVB_NORM_LAYER 2     /* (x-mean)*rsqrt(var+eps)*w + b              */
+#define FVB_NORM_RMS 3       /* x*rsqrt(mean(x^2)+eps), no weight (fvb_norm_bf16) */
+#define FVB_NORM_ADA_STYLE 4 /* x*rsqrt(mean(x^2)+eps)*(1+scale)+shift, gate out  */
 
 typedef struct fvb_gemm_args {
   /* C[M,N] = A[M,K] * B[N,K]^T, bf16 operands, f32 accumulation.         */
@@ -113,6 +115,22 @@ typedef struct fvb_gemm_args {
    * token operand.  Swapped orientation only (a = weights), epilogues
    * FVB_EPI_GEGLU and FVB_EPI_F32_ACC, block_n 0 (= 208) or 208.          */
   int32_t pair;
+  /* FVB_EPI_BF16, normal orientation, one K split: per-element operands of
+   * the reference's bf16 residual epilogues (matmul_small_res /
+   * matmul_small_res_gate matmul_triton_ops.py:548,713; the cublasLt bias +
+   * residual of matmul_bias_forward_cuda.cu):
+   *   out = bf16(res + gate_tok * act(alpha*acc + bias))
+   * res, gate_tok: bf16 [m, ld] or NULL; res may alias out; rows 16-byte
+   * aligned, n a multiple of 8.                                             */
+  const void* res;
+  int64_t ld_res;
+  const void* gate_tok;
+  int64_t ld_gate_tok;
+  /* FVB_EPI_QKV_ROPE, normal orientation: rotated q / k stored with each
+   * rotary pair adjacent (dims 2i, 2i+1 — the layout of the reference's
+   * Triton kernels, attention_triton_ops.py:149-214) instead of rotate-half
+   * order (dims i, i + head_dim/2).                                         */
+  int32_t rope_interleaved;
 } fvb_gemm_args;
 
 /* tcgen05/TMEM tensor-core GEMM with fused epilogues.
@@ -251,6 +269,24 @@ int fvb_norm(int32_t mode, const float* x, int64_t ld_in, void* out,
              int64_t ld_out, int32_t out_f32, int32_t rows, int32_t dim,
              const void* w, const void* b, const float* mod, float eps,
              void* stream);
+
+/* Row normalisation of bf16 input rows, the reference Triton norms on its
+ * bf16 activation buffers (rows [rows, dim], strides in elements, dim a
+ * multiple of 8, rows 16-byte aligned), bf16 output:
+ *   FVB_NORM_RMS:       out = x * rsqrt(mean(x^2) + eps)   (rms_norm_kernel
+ *                       norm_triton_ops.py:317; (1+w) is folded into the
+ *                       next GEMM's weights by the reference's packer)
+ *   FVB_NORM_LAYER:     out = (x - mean) * rsqrt(var + eps) * w + b
+ *                       (layer_norm_small_kernel :90), w, b bf16 [dim]
+ *   FVB_NORM_ADA_STYLE: out = x * rsqrt(mean(x^2) + eps) * (1 + scale) + shift
+ *                       and gate_out[row] = gate, where (scale | shift | gate)
+ *                       = style[0 .. 3*dim) bf16, the first style row for every
+ *                       row as in adarms_norm_kernel :355; gate_out bf16
+ *                       [rows, ld_gate].                                      */
+int fvb_norm_bf16(int32_t mode, const void* x, int64_t ld_in, void* out,
+                  int64_t ld_out, int32_t rows, int32_t dim, const void* w,
+                  const void* b, const void* style, void* gate_out,
+                  int64_t ld_gate, float eps, void* stream);
 
 /* Image normalisation + patch extraction: uint8 HWC images [views, H, W, 3]
  * -> bf16 patch rows [views*(H/p)*(W/p), ldo] with column c*p*p + ky*p + kx

@@ -1,0 +1,30 @@
+"""The atomic_ops drop-in keeps the reference's operator names and
+signatures (fixture recorded from fluxvla/ops/atomic_ops.py by
+tests/golden/make_atomic_ops_signatures.py)."""
+import inspect
+import json
+import os
+
+import pytest
+
+from fluxvla_b200 import atomic_ops
+
+SIGS = json.load(open(os.path.join(os.path.dirname(__file__), 'golden',
+                                   'atomic_ops_signatures.json')))
+
+
+def test_fixture_covers_the_pi05_import_list():
+    assert len(SIGS) == 17
+
+
+@pytest.mark.parametrize('name', sorted(SIGS))
+def test_signature_matches_reference(name):
+    fn = getattr(atomic_ops, name)
+    params = list(inspect.signature(fn).parameters.values())
+    assert [p.name for p in params] == SIGS[name]['args']
+    for p in params:
+        if p.name in SIGS[name]['defaults']:
+            assert p.default == SIGS[name]['defaults'][p.name], p.name
+        else:
+            assert p.default is inspect.Parameter.empty, p.name
+    assert f'atomic_ops.py:{SIGS[name]["line"]}' in fn.__doc__
