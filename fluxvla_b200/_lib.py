@@ -85,6 +85,9 @@ EXPORTS = {
     'fvb_attention': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),
     'fvb_attention_workspace_bytes': (C.c_int64, [C.POINTER(AttnArgs)]),
     'fvb_attention_combine': (C.c_int, [C.POINTER(AttnArgs), C.c_void_p]),
+    'fvb_softmax_rows': (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32,
+                                   C.c_int32, C.c_void_p, C.c_void_p, C.c_int64,
+                                   C.c_void_p]),
     'fvb_norm_bf16': (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_void_p,
                                 C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,

@@ -447,4 +447,44 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Row softmax of materialised attention logits (fvb_softmax_rows): f32
+// logits [rows, keys] -> bf16 probabilities.  Key j takes part when
+// j >= n_prefix (suffix keys) or j < min(valid_prefix, n_prefix); masked
+// keys hold the reference's large negative value, so a row with every key
+// masked comes out uniform as in the reference kernels.  One warp per row.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    softmax_rows_kernel(const float* __restrict__ in, long long ld_in, int rows,
+                        int keys, int n_prefix, const int* __restrict__ valid_prefix,
+                        bf16* __restrict__ out, long long ld_out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float big_neg = -2.3819763e38f;
+  const int vl = max(0, min(*valid_prefix, n_prefix));
+  const float* x = in + (long long)row * ld_in;
+  float mx = big_neg;
+  for (int j = lane; j < keys; j += 32) {
+    const bool ok = j >= n_prefix || j < vl;
+    mx = fmaxf(mx, ok ? x[j] : big_neg);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+  for (int j = lane; j < keys; j += 32) {
+    const bool ok = j >= n_prefix || j < vl;
+    sum += __expf((ok ? x[j] : big_neg) - mx);
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.f / sum;
+  bf16* o = out + (long long)row * ld_out;
+  for (int j = lane; j < keys; j += 32) {
+    const bool ok = j >= n_prefix || j < vl;
+    o[j] = __float2bfloat16(__expf((ok ? x[j] : big_neg) - mx) * inv);
+  }
+}
+
 }  // namespace fvb

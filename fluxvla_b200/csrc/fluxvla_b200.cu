@@ -754,6 +754,18 @@ int fvb_norm_bf16(int32_t mode, const void* x, int64_t ld_in, void* out,
                   (long long)ld_gate, eps);
 }
 
+int fvb_softmax_rows(const float* logits, int64_t ld_in, int32_t rows,
+                     int32_t keys, int32_t n_prefix, const int32_t* valid_prefix,
+                     void* out, int64_t ld_out, void* stream) {
+  if (!logits || !out || !valid_prefix || rows <= 0 || keys <= 0 || n_prefix < 0 ||
+      n_prefix > keys || ld_in < keys || ld_out < keys)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_softmax_rows: bad arguments");
+  return launch_k("fvb_softmax_rows", fvb::softmax_rows_kernel, dim3((rows + 7) / 8),
+                  dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), logits,
+                  (long long)ld_in, (int)rows, (int)keys, (int)n_prefix,
+                  (const int*)valid_prefix, (bf16*)out, (long long)ld_out);
+}
+
 int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
                  int32_t width, int32_t patch, const float* mean3,
                  const float* std3, void* out, int64_t ldo, void* stream) {

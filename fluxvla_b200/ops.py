@@ -156,6 +156,20 @@ def norm_bf16(mode: int, x: torch.Tensor, out: torch.Tensor, *, w=None,
         eps, _stream()))
 
 
+def softmax_rows(logits: torch.Tensor, out: torch.Tensor, *, n_prefix: int,
+                 valid_prefix: torch.Tensor) -> None:
+    """bf16 out = softmax over the attended keys of f32 logits rows
+    (fvb_softmax_rows); valid_prefix: int32 device tensor of one value."""
+    if valid_prefix.dtype != torch.int32 or not valid_prefix.is_cuda:
+        raise TypeError('valid_prefix: expected an int32 CUDA tensor')
+    ld_in = _rowmajor(logits, 'logits', F32)
+    ld_out = _rowmajor(out, 'out', BF16)
+    rows, keys = logits.shape
+    check(_lib.lib().fvb_softmax_rows(_ptr(logits), ld_in, rows, keys, n_prefix,
+                                      _ptr(valid_prefix), _ptr(out), ld_out,
+                                      _stream()))
+
+
 def norm(mode: int, x: torch.Tensor, out: torch.Tensor, *, w=None, b=None,
          mod=None, eps: float = 1e-6) -> None:
     ld_in = _rowmajor(x, 'x', F32)

@@ -288,6 +288,17 @@ int fvb_norm_bf16(int32_t mode, const void* x, int64_t ld_in, void* out,
                   const void* b, const void* style, void* gate_out,
                   int64_t ld_gate, float eps, void* stream);
 
+/* Row softmax of materialised attention logits, for callers that keep the
+ * reference's unfused attention (matmul_abT_scale -> softmax -> P.V):
+ * f32 logits [rows, keys] (row stride ld_in) -> bf16 probabilities [rows,
+ * ld_out].  Key j is attended when j >= n_prefix or j < min(*valid_prefix,
+ * n_prefix) (valid_prefix: one int32 in device memory).  n_prefix = keys
+ * gives softmax_kernel_masklen, n_prefix < keys softmax_kernel_prefix_suffix
+ * (fluxvla/ops/triton/attention_triton_ops.py:81,111).                    */
+int fvb_softmax_rows(const float* logits, int64_t ld_in, int32_t rows,
+                     int32_t keys, int32_t n_prefix, const int32_t* valid_prefix,
+                     void* out, int64_t ld_out, void* stream);
+
 /* Image normalisation + patch extraction: uint8 HWC images [views, H, W, 3]
  * -> bf16 patch rows [views*(H/p)*(W/p), ldo] with column c*p*p + ky*p + kx
  * holding (x - mean[c]) / (std[c] + 1e-8); columns >= 3*p*p are zeroed.

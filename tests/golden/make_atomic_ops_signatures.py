@@ -1,6 +1,7 @@
 """Record the signatures of the reference operators that
-fluxvla_b200.atomic_ops replaces (the functions pi05_flowmatching_inference.py
-imports from fluxvla/ops/atomic_ops.py) as a JSON fixture.
+fluxvla_b200.atomic_ops and fluxvla_b200.attention_triton_ops replace (the
+functions pi05_flowmatching_inference.py imports from fluxvla/ops/atomic_ops.py
+and from fluxvla/ops/triton/attention_triton_ops.py) as a JSON fixture.
 
 Run in a checkout that has the reference tree:
     python tests/golden/make_atomic_ops_signatures.py <fluxvla root>
@@ -27,6 +28,23 @@ for node in tree.body:
         names = [x.arg for x in a.args]
         defaults = [ast.literal_eval(d) for d in a.defaults]
         sigs[node.name] = {
+            'args': names,
+            'defaults': dict(zip(names[len(names) - len(defaults):], defaults)),
+            'line': node.lineno}
+# the Triton attention kernels pi05_flowmatching_inference.py launches itself
+att = ast.parse(open(os.path.join(
+    root, 'fluxvla/ops/triton/attention_triton_ops.py')).read())
+direct = set()
+for node in ast.walk(inf):
+    if isinstance(node, ast.ImportFrom) and node.module == \
+            'fluxvla.ops.triton.attention_triton_ops':
+        direct |= {a.name for a in node.names}
+for node in att.body:
+    if isinstance(node, ast.FunctionDef) and node.name in direct:
+        a = node.args
+        names = [x.arg for x in a.args]
+        defaults = [ast.literal_eval(d) for d in a.defaults]
+        sigs['triton:' + node.name] = {
             'args': names,
             'defaults': dict(zip(names[len(names) - len(defaults):], defaults)),
             'line': node.lineno}

@@ -269,3 +269,52 @@ def test_weight_cache_follows_in_place_updates():
     w.copy_(rn(256, 128, seed=52, scale=0.02))  # bumps the version
     A.matmul_bias_small(a, w, b, out, 256, 128)
     close(out, a.float() @ w.float(), 'updated weights')
+
+
+# ---------------------------------------------------------------------------
+# the unfused attention trio that pi05_flowmatching_inference.py launches
+# directly (attention_triton_ops.py:5,81,111), with the Triton launch syntax
+# ---------------------------------------------------------------------------
+from fluxvla_b200 import attention_triton_ops as T  # noqa: E402
+
+
+def masked_softmax_ref(lg, n_prefix, valid):
+    keys = lg.shape[1]
+    j = torch.arange(keys, device=dev)
+    ok = (j >= n_prefix) | (j < min(max(valid, 0), n_prefix))
+    return torch.softmax(torch.where(ok[None], lg, torch.full_like(lg, -2.3819763e38)), -1)
+
+
+@pytest.mark.parametrize('valid', [E, 150, 0])
+def test_prefix_attention_trio(valid):
+    Q = rn(E * NH, HD, seed=60)
+    Kc = rn(E, HD, seed=61)
+    Vc = rn(E, HD, seed=62)
+    logits = torch.zeros(E * NH, E, device=dev)
+    probs = torch.zeros(E * NH, E, dtype=bf, device=dev)
+    vlen = torch.tensor([valid], dtype=torch.int32, device=dev)
+    T.matmul_abT_scale[(999,)](Q, Kc, logits, E * NH, E, HD, 1.0 / 16,
+                               BLOCK_SIZE_M=32, BLOCK_SIZE_N=32, BLOCK_SIZE_K=64)
+    lref = Q.float() @ Kc.float().t() / 16
+    close(logits, lref, 'matmul_abT_scale')
+    T.softmax_kernel_masklen[(1,)](logits, E * NH, E, vlen, probs, BLOCK_SIZE_M=4,
+                                   BLOCK_SIZE=1024)
+    close(probs, masked_softmax_ref(logits, E, valid), 'softmax_kernel_masklen')
+    ctx = torch.empty(E * NH, HD, dtype=bf, device=dev)
+    A.matmul_attn_v(probs, Vc, ctx, head_dim=HD)
+    close(ctx, probs.float() @ Vc.float(), 'P.V')
+
+
+def test_suffix_attention_trio():
+    pre = 816
+    Q = rn(S * NH, HD, seed=63)
+    Kc = rn(pre + S, HD, seed=64)
+    logits = torch.zeros(S * NH, pre + S, device=dev)
+    probs = torch.zeros(S * NH, pre + S, dtype=bf, device=dev)
+    vlen = torch.tensor([700], dtype=torch.int32, device=dev)
+    T.matmul_abT_scale[(1,)](Q, Kc, logits, S * NH, pre + S, HD, 256 ** -0.5)
+    close(logits, Q.float() @ Kc.float().t() / 16, 'matmul_abT_scale (ragged N)')
+    T.softmax_kernel_prefix_suffix[(1,)](logits, S * NH, pre, S, vlen, probs)
+    p = probs.float()
+    close(p, masked_softmax_ref(logits, pre, 700), 'softmax_kernel_prefix_suffix')
+    assert p[:, 700:pre].abs().max() == 0 and p[:, pre:].min() > 0
