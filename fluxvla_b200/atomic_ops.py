@@ -211,9 +211,10 @@ def matmul_split_k_bias_res(x, weight, bias, res, out, buf, num_patches,
 def layer_norm_matmul_bias(x, norm_w, norm_b, proj_w, proj_b, out, x_norm,
                            num_patches, in_features, out_features, eps=1e-5):
     """atomic_ops.py:117 — LayerNorm(eps) then out = x_norm @ W + b."""
-    xn = _rows(x_norm, in_features)
-    _ln(_rows(x, in_features), norm_w, norm_b, xn, eps)
-    _linear(xn, proj_w, _rows(out, out_features), bias=proj_b)
+    x2 = _rows(x, in_features)
+    xn = _rows(x_norm, in_features)[:x2.shape[0]]
+    _ln(x2, norm_w, norm_b, xn, eps)
+    _linear(xn, proj_w, _rows(out, out_features)[:x2.shape[0]], bias=proj_b)
 
 
 # ---------------------------------------------------------------------------
