@@ -340,13 +340,6 @@ __device__ void attention_item(const Params& p, int layer, int item,
   bar128();  // the region is reused by the next item
 }
 
-// s_rstd[t] = 1/sqrt(ss[t]/width + eps) for the CTA (all worker threads sync)
-__device__ __forceinline__ void load_rstd(const Params& p, const float* ss,
-                                          float* s_rstd, int wtid) {
-  if (wtid < TOK) s_rstd[wtid] = rsqrtf(__ldcg(ss + min(wtid, p.n_tok - 1)) / p.width + p.eps);
-  bar128();
-}
-
 // xs[t,k] = bf16(x[t,k]*scale[k]) and ss[t] += sum_k x[t,k]^2, spread over
 // the grid (8 values per thread; a warp covers 256 values of one token)
 __device__ void prep_scaled(const Params& p, const float* scale, float* ss,
@@ -378,36 +371,56 @@ __device__ void prep_scaled(const Params& p, const float* scale, float* ss,
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// hb[t,i] = bf16(gelu(rs*g + bg) * (rs*u + bu)), (g,u) = acc_gu[t, 2i..2i+1]
-__device__ void prep_geglu(const Params& p, const float* gub, const float* s_rstd,
-                           int wtid) {
+// Per-token rstd of the phase's RMSNorm into shared memory.  The sums of
+// squares are loaded (`ssv`, issued by the caller before its first batch of
+// operand loads so that both round trips overlap) and stored once per CTA:
+// read per task from global memory, the whole grid would queue on the few
+// L2 lines that hold them.
+__device__ __forceinline__ float issue_ss(const Params& p, const float* ss, int wtid) {
+  return wtid < TOK ? __ldcg(ss + min(wtid, p.n_tok - 1)) : 0.f;
+}
+__device__ __forceinline__ void publish_rstd(const Params& p, float ssv, float* s_rstd,
+                                             int wtid) {
+  if (wtid < TOK) s_rstd[wtid] = rsqrtf(ssv / p.width + p.eps);
+  bar128();
+}
+
+// hb[t,i] = bf16(gelu(rs*g + bg) * (rs*u + bu)), (g,u) = acc_gu[t, 2i..2i+1],
+// rs = rstd of ss_post
+__device__ void prep_geglu(const Params& p, const float* gub, const float* ss,
+                           float* s_rstd, int wtid) {
   const int per_tok = p.mlp / 8;
   const int total = p.n_tok * per_tok;
   const int ld = 2 * p.mlp;
   constexpr int PB = 2;
-  for (int base = blockIdx.x * 128 + wtid; base < total; base += gridDim.x * 128 * PB) {
-    float4 q[PB][4];
-    float rs[PB];
+  const int stride = gridDim.x * 128;
+  float4 q[PB][4];
+  auto load = [&](int base) {
 #pragma unroll
     for (int u = 0; u < PB; ++u) {
-      const int c = base + u * gridDim.x * 128;
-      rs[u] = 0.f;
+      const int c = base + u * stride;
 #pragma unroll
       for (int h = 0; h < 4; ++h) q[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (c < total) {
         const int t = c / per_tok, i0 = (c % per_tok) * 8;
-        rs[u] = s_rstd[t];
         const float* src = p.acc_gu + (long long)t * ld + 2 * i0;
 #pragma unroll
         for (int h = 0; h < 4; ++h) q[u][h] = ldcg4(src + 4 * h);
       }
     }
+  };
+  const int base0 = blockIdx.x * 128 + wtid;
+  const float ssv = issue_ss(p, ss, wtid);
+  load(base0);
+  publish_rstd(p, ssv, s_rstd, wtid);
+  for (int base = base0; base < total; base += stride * PB) {
+    if (base != base0) load(base);
 #pragma unroll
     for (int u = 0; u < PB; ++u) {
-      const int c = base + u * gridDim.x * 128;
+      const int c = base + u * stride;
       if (c >= total) break;
       const int t = c / per_tok, i0 = (c % per_tok) * 8;
-      const float r = rs[u];
+      const float r = s_rstd[t];
       float y[8];
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
@@ -429,28 +442,27 @@ __device__ void prep_geglu(const Params& p, const float* gub, const float* s_rst
 }
 
 // q = rope(rstd*acc_q + b), k = rope(rstd*acc_k + b), v = rstd*acc_v + b for
-// the suffix tokens, written once as bf16 for every attention item.
-// Task (t, i): i < (H+1)*hd/2 is a rotary pair of a query head or the key
-// head, otherwise a pair (d, d + hd/2) of the value head.
-__device__ void finalize_qkv(const Params& p, int layer, const float* s_rstd, int wtid) {
+// the suffix tokens, written once as bf16 for every attention item; rstd of
+// ss_in.  Task (t, i): i < (H+1)*hd/2 is a rotary pair of a query head or
+// the key head, otherwise a pair (d, d + hd/2) of the value head.
+__device__ void finalize_qkv(const Params& p, int layer, const float* ss, float* s_rstd,
+                             int wtid) {
   const int H = p.heads, hd = p.hd, half = hd >> 1;
   const int qkv_ld = (H + 2) * hd;
   const int per_tok = (H + 2) * half;
   const int total = p.n_tok * per_tok;
   const float* bias = p.qkv_bias ? p.qkv_bias + (long long)layer * qkv_ld : nullptr;
   constexpr int FB = 4;
-  for (int base = blockIdx.x * 128 + wtid; base < total; base += gridDim.x * 128 * FB) {
-    float2 a[FB], cs[FB];
-    float rs[FB];
+  const int stride = gridDim.x * 128;
+  float2 a[FB], cs[FB];
+  auto load = [&](int base) {
 #pragma unroll
     for (int u = 0; u < FB; ++u) {
-      const int c = base + u * gridDim.x * 128;
+      const int c = base + u * stride;
       a[u] = cs[u] = make_float2(0.f, 0.f);
-      rs[u] = 0.f;
       if (c < total) {
         const int t = c / per_tok, i = c % per_tok;
         const float* row = p.acc_qkv + (long long)t * qkv_ld;
-        rs[u] = s_rstd[t];
         if (i < (H + 1) * half) {
           const int hh = i / half, ii = i % half;
           a[u] = __ldcg(reinterpret_cast<const float2*>(row + hh * hd + 2 * ii));
@@ -463,12 +475,19 @@ __device__ void finalize_qkv(const Params& p, int layer, const float* s_rstd, in
         }
       }
     }
+  };
+  const int base0 = blockIdx.x * 128 + wtid;
+  const float ssv = issue_ss(p, ss, wtid);
+  load(base0);
+  publish_rstd(p, ssv, s_rstd, wtid);
+  for (int base = base0; base < total; base += stride * FB) {
+    if (base != base0) load(base);
 #pragma unroll
     for (int u = 0; u < FB; ++u) {
-      const int c = base + u * gridDim.x * 128;
+      const int c = base + u * stride;
       if (c >= total) break;
       const int t = c / per_tok, i = c % per_tok;
-      const float r = rs[u];
+      const float r = s_rstd[t];
       if (i < (H + 1) * half) {
         const int hh = i / half, ii = i % half;
         float x1 = r * a[u].x, x2 = r * a[u].y;
@@ -679,8 +698,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (cta == 0 && wtid < TOK) p.ss_post[wtid] = 0.f;
           prep_scaled(p, p.in_scale + (long long)l * p.width, p.ss_in, wtid);
         } else if (ph == 2) {
-          load_rstd(p, p.ss_in, s_rstd, wtid);
-          finalize_qkv(p, l, s_rstd, wtid);
+          finalize_qkv(p, l, p.ss_in, s_rstd, wtid);
         } else if (ph == 3) {
           for (int w = cta; w < p.heads * p.nkb; w += G)
             attention_item(p, l, w, region, wtid, tr && l == 0 && w == cta);
@@ -693,9 +711,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (ph == 6) {
           prep_scaled(p, p.post_scale + (long long)l * p.width, p.ss_post, wtid);
         } else if (ph == 8) {
-          load_rstd(p, p.ss_post, s_rstd, wtid);
-          prep_geglu(p, p.gu_bias ? p.gu_bias + (long long)l * 2 * p.mlp : nullptr, s_rstd,
-                     wtid);
+          prep_geglu(p, p.gu_bias ? p.gu_bias + (long long)l * 2 * p.mlp : nullptr,
+                     p.ss_post, s_rstd, wtid);
         } else {
           const int gi = ph == 1 ? 0 : (ph == 5 ? 1 : (ph == 7 ? 2 : 3));
           const Gemm& g = p.g[gi];
