@@ -560,6 +560,7 @@ class PI0EngineB200:
     def _set_masks(self, key_valid_cpu: torch.Tensor):
         """Positions and key mask from the prefix pad mask
         (pi0_flowmatching.py:730 and :817-819)."""
+        self._last_key_valid = key_valid_cpu.to(torch.bool).clone()
         kv = key_valid_cpu.to(torch.int64)
         pos = (torch.cumsum(kv, 0) - 1).clamp(min=0).to(torch.int32)
         self.B['key_valid'].copy_(kv.to(torch.uint8))
@@ -587,7 +588,11 @@ class PI0EngineB200:
                 else lang_masks.reshape(-1).bool().cpu()
             kv = torch.cat([im.repeat_interleave(cfg.tokens_per_view), lm])
             assert kv.numel() == self.E, (kv.numel(), self.E)
-            self._set_masks(kv)
+            # positions / key mask / suffix rotary rows depend only on the
+            # padding pattern: rebuilt only when it changes
+            last = getattr(self, '_last_key_valid', None)
+            if last is None or not torch.equal(last, kv):
+                self._set_masks(kv)
         if state is not None and cfg.has_state_token:
             B['state'].copy_(state.reshape(1, -1), non_blocking=True)
         if noise is not None:
@@ -643,4 +648,10 @@ class PI0EngineB200:
         if self.graph is None:
             self.capture(prefix=self.has_vision or self.has_llm)
         self.replay()
-        return self.B['x_t'].to('cpu').reshape(1, self.A, -1)
+        # read back through a pinned buffer on the engine's stream
+        if getattr(self, '_x_host', None) is None:
+            self._x_host = torch.empty(self.B['x_t'].shape, dtype=self.B['x_t'].dtype,
+                                       pin_memory=True)
+        self._x_host.copy_(self.B['x_t'], non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return self._x_host.clone().reshape(1, self.A, -1)
