@@ -37,9 +37,10 @@ constexpr int TOK = 64;                    // MMA N (tokens, padded)
 constexpr int A_BYTES = 128 * 64 * 2;      // weight k-tile (16 KB)
 constexpr int BKT_BYTES = TOK * 64 * 2;    // B k-tile (8 KB)
 constexpr int MAX_KT = 8;                  // k-tiles per work item
-constexpr int APITCH = 264;                // attention smem row pitch (bf16)
-constexpr int ATILE = 64 * APITCH;         // elements per attention tile
-constexpr int REGION_BYTES = 3 * ATILE * 2 + 64 + 64 * 4 + 2 * 64 * 4;  // >= MAX_KT*BKT
+// attention tiles: 64 rows x 256 dims bf16 as four 64-column TMA boxes,
+// 128-byte swizzled (8 KB each), Q | K | V back to back
+constexpr int ATT_TILE_BYTES = 64 * 256 * 2;
+constexpr int REGION_BYTES = 3 * ATT_TILE_BYTES + 64 + 64 * 4 + 2 * 64 * 4;  // >= MAX_KT*BKT
 constexpr int SMEM_BYTES = 1024 + STAGES * A_BYTES + REGION_BYTES + 256 + TOK * 4;
 constexpr int N_GEMM = 4;  // QKV, O, GU, DOWN
 
@@ -63,8 +64,8 @@ struct Params {
   const float* down_gate;   // [L, width] or null
   float eps;
   float* x;                 // residual [n_tok, width] f32
-  const bf16* kc;           // [L, cache_rows, hd]
-  const bf16* vc;
+  bf16* kc;                 // [L, cache_rows, hd]: prefix rows read, the
+  bf16* vc;                 // suffix rows n_prefix.. written each step
   long long cache_layer;    // elements per layer of the cache
   const uint8_t* key_valid;
   const int* blocks;
@@ -83,7 +84,6 @@ struct Params {
   bf16* qb;        // [TOK, heads*hd] rotated queries (rows >= n_tok zero)
   bf16* xs;        // [TOK, width] x*(1+w) for the QKV / gate-up B operand
   bf16* hb;        // [TOK, mlp] gelu(g)*u for the down B operand
-  bf16* kvs;       // [2][128, hd] suffix keys (rotated) / values (rows >= n_tok zero)
   unsigned* bar;   // [0..1] 64-bit arrival count, [BAR_ABORT] abort flag
   int nkb;         // key blocks of 64
   int trace;       // diagnostics: phase stamps of layer 0 in g_mega_trace
@@ -180,40 +180,54 @@ __device__ __forceinline__ int b_off(int t, int kc) {
 // ---------------------------------------------------------------------------
 // attention block: 64 query rows (one head) x one 64-key block
 // ---------------------------------------------------------------------------
+// byte offset of element (row, col) of a 64 x 256 attention tile stored as
+// four 64-column, 128-byte-swizzled TMA boxes (col a multiple of 8)
+__device__ __forceinline__ uint32_t att_off(int row, int col) {
+  return (uint32_t)((col >> 6) * 8192 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map,
+                                            int32_t x, int32_t y, int32_t z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// attention block: 64 query rows (one head) x one 64-key block.  Operands by
+// TMA: the rotated queries of head h (qb), and 64 keys / values from the
+// layer's cache rows (prefix rows from the prefill, suffix rows written by
+// the finalize phase; rows past the cache are zero-filled), completing on
+// a_full (phase a_par).
+// ---------------------------------------------------------------------------
 __device__ void attention_item(const Params& p, int layer, int item,
-                               uint8_t* region, int wtid, bool tr) {
-  const int H = p.heads, hd = p.hd, half = hd >> 1;
+                               uint8_t* region, uint64_t* a_full, uint32_t a_par,
+                               const CUtensorMap* tm_q, const CUtensorMap* tm_k,
+                               const CUtensorMap* tm_v, int wtid, bool tr) {
+  const int hd = p.hd;
   const int h = item / p.nkb, kb = item % p.nkb;
   const int S = p.n_tok, E = p.n_prefix, n_kv = E + S;
-  const int qkv_ld = (H + 2) * hd;
-  bf16* sQ = reinterpret_cast<bf16*>(region);
-  bf16* sK = sQ + ATILE;
-  bf16* sV = sK + ATILE;
-  uint8_t* sMask = reinterpret_cast<uint8_t*>(sV + ATILE);
+  uint8_t* sQ = region;
+  uint8_t* sK = region + ATT_TILE_BYTES;
+  uint8_t* sV = region + 2 * ATT_TILE_BYTES;
+  uint8_t* sMask = region + 3 * ATT_TILE_BYTES;
   int* sKb = reinterpret_cast<int*>(sMask + 64);
-  const float* bias = p.qkv_bias ? p.qkv_bias + (long long)layer * qkv_ld : nullptr;
-  const bf16* kc = p.kc + layer * p.cache_layer;
-  const bf16* vc = p.vc + layer * p.cache_layer;
 
-  // operands: rotated queries of head h, prefix keys/values from the cache,
-  // suffix keys/values from the finalized buffers; rows past the end zero
   const int key0 = kb * 64;
-  const bf16* ks = p.kvs;
-  const bf16* vs = p.kvs + 128 * hd;
-  for (int c = wtid; c < 64 * (hd / 8); c += 128) {
-    const int r = c / (hd / 8), cc = c % (hd / 8);
-    cp_async16(sQ + r * APITCH + cc * 8,
-               p.qb + (long long)r * H * hd + h * hd + cc * 8, true);
-    const int key = key0 + r;
-    const bool pre = key < E;
-    const int sr = key - E;
-    const bool suf = !pre && sr < 128;
-    const bf16* kk = pre ? kc + (long long)key * hd : (suf ? ks + sr * hd : ks);
-    const bf16* vv = pre ? vc + (long long)key * hd : (suf ? vs + sr * hd : vs);
-    cp_async16(sK + r * APITCH + cc * 8, kk + cc * 8, pre || suf);
-    cp_async16(sV + r * APITCH + cc * 8, vv + cc * 8, pre || suf);
+  if (wtid == 0) {
+    mbar_arrive_expect_tx(a_full, 3 * ATT_TILE_BYTES);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      tma_load_2d(sQ + c * 8192, tm_q, h * hd + c * 64, 0, a_full);
+      tma_load_3d(sK + c * 8192, tm_k, c * 64, key0, layer, a_full);
+      tma_load_3d(sV + c * 8192, tm_v, c * 64, key0, layer, a_full);
+    }
   }
-  cp_async_commit();
+  __syncwarp();
   if (wtid < 64) {
     const int key = key0 + wtid;
     uint8_t vis = key < n_kv;
@@ -225,7 +239,9 @@ __device__ void attention_item(const Params& p, int layer, int item,
     sMask[wtid] = vis;
     sKb[wtid] = kbv;
   }
-  cp_async_wait<0>();
+  // a wait that gives up has set the abort flag: the step's output is then
+  // discarded, so the block is still computed (uniform control flow)
+  wait_bar(p, a_full, a_par);
   bar128();
   if (tr) g_mega_trace[blockIdx.x][24] = globaltimer_ns();
 
@@ -241,14 +257,14 @@ __device__ void attention_item(const Params& p, int layer, int item,
 #pragma unroll 4
   for (int kk = 0; kk < 256 / 16; ++kk) {
     uint32_t a0, a1, a2, a3;
-    ldsm_x4(sQa + ((warp * 16 + (lane & 15)) * APITCH + kk * 16 + (lane >> 4) * 8) * 2,
+    ldsm_x4(sQa + att_off(warp * 16 + (lane & 15), kk * 16 + (lane >> 4) * 8),
             a0, a1, a2, a3);
 #pragma unroll
     for (int nt = 0; nt < 8; nt += 2) {
       uint32_t b0, b1, b2, b3;
       const int mi = lane >> 3, rr = lane & 7;
       const int key = nt * 8 + (mi >> 1) * 8 + rr;
-      ldsm_x4(sKa + (key * APITCH + kk * 16 + (mi & 1) * 8) * 2, b0, b1, b2, b3);
+      ldsm_x4(sKa + att_off(key, kk * 16 + (mi & 1) * 8), b0, b1, b2, b3);
       mma_bf16_16816(s[nt], a0, a1, a2, a3, b0, b1);
       mma_bf16_16816(s[nt + 1], a0, a1, a2, a3, b2, b3);
     }
@@ -316,7 +332,7 @@ __device__ void attention_item(const Params& p, int layer, int item,
         const int mi = lane >> 3, rr = lane & 7;
         const int key = kk * 16 + (mi & 1) * 8 + rr;
         const int col = dp * 64 + nt * 8 + (mi >> 1) * 8;
-        ldsm_x4_t(sVa + (key * APITCH + col) * 2, b0, b1, b2, b3);
+        ldsm_x4_t(sVa + att_off(key, col), b0, b1, b2, b3);
         mma_bf16_16816(o[nt], a0, a1, a2, a3, b0, b1);
         mma_bf16_16816(o[nt + 1], a0, a1, a2, a3, b2, b3);
       }
@@ -337,7 +353,9 @@ __device__ void attention_item(const Params& p, int layer, int item,
     if (r1 < S) __stcg(reinterpret_cast<float2*>(pml + r1 * 2), make_float2(mx1, l1));
   }
   if (tr) g_mega_trace[blockIdx.x][26] = globaltimer_ns();
-  bar128();  // the region is reused by the next item
+  // the region is reused by the next item's TMA loads (async proxy)
+  fence_async_smem();
+  bar128();
 }
 
 // xs[t,k] = bf16(x[t,k]*scale[k]) and ss[t] += sum_k x[t,k]^2, spread over
@@ -494,19 +512,22 @@ __device__ void finalize_qkv(const Params& p, int layer, const float* ss, float*
         if (bias) { x1 += bias[hh * hd + 2 * ii]; x2 += bias[hh * hd + 2 * ii + 1]; }
         const float o1 = x1 * cs[u].x - x2 * cs[u].y;
         const float o2 = x2 * cs[u].x + x1 * cs[u].y;
-        bf16* dst = hh < H ? p.qb + (long long)t * H * hd + hh * hd : p.kvs + t * hd;
+        bf16* dst = hh < H ? p.qb + (long long)t * H * hd + hh * hd
+                           : p.kc + layer * p.cache_layer + (long long)(p.n_prefix + t) * hd;
         dst[ii] = __float2bfloat16(o1);
         dst[ii + half] = __float2bfloat16(o2);
       } else {
         const int d = i - (H + 1) * half;
         float v1 = r * a[u].x, v2 = r * a[u].y;
         if (bias) { v1 += bias[(H + 1) * hd + d]; v2 += bias[(H + 1) * hd + d + half]; }
-        bf16* dst = p.kvs + 128 * hd + t * hd;
+        bf16* dst = p.vc + layer * p.cache_layer + (long long)(p.n_prefix + t) * hd;
         dst[d] = __float2bfloat16(v1);
         dst[d + half] = __float2bfloat16(v2);
       }
     }
   }
+  // the attention phase reads q, k and v through TMA (async proxy)
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // merge of the key-block partials of one (head, token) row -> attn (bf16)
@@ -575,6 +596,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                        const __grid_constant__ CUtensorMap tb_xs,
                        const __grid_constant__ CUtensorMap tb_attn,
                        const __grid_constant__ CUtensorMap tb_h,
+                       const __grid_constant__ CUtensorMap ta_q,
+                       const __grid_constant__ CUtensorMap ta_k,
+                       const __grid_constant__ CUtensorMap ta_v,
                        const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -586,7 +610,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* b_full = empty + STAGES;
   uint64_t* t_full = b_full + 1;
   uint64_t* t_empty = t_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 1);
+  uint64_t* a_full = t_empty + 1;  // attention operands landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_full + 1);
   // per-token rstd of the phase's RMSNorm, loaded once per CTA and phase:
   // read per task from global memory, the whole grid would queue on the
   // few L2 lines that hold the sums of squares
@@ -602,6 +627,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(b_full, 1);
     mbar_init(t_full, 1);
     mbar_init(t_empty, 4);
+    mbar_init(a_full, 1);
     fence_barrier_init();
     prefetch_tensormap(&tm_qkv);
     prefetch_tensormap(&tm_o);
@@ -610,6 +636,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tensormap(&tb_xs);
     prefetch_tensormap(&tb_attn);
     prefetch_tensormap(&tb_h);
+    prefetch_tensormap(&ta_q);
+    prefetch_tensormap(&ta_k);
+    prefetch_tensormap(&ta_v);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 64);
   tc_fence_before();
@@ -684,6 +713,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int qkv_ld = (p.heads + 2) * p.hd;
     int j = 0;
     const bool tr = p.trace && wtid == 0 && cta < 256;
+    uint32_t a_items = 0;  // attention items run by this CTA (a_full phases)
     if (tr) g_mega_trace[cta][0] = globaltimer_ns();
     for (int l = 0; l < p.n_layers; ++l) {
       // phases: 0 prep QKV operand, 1 QKV, 2 finalize q/k/v, 3 attention,
@@ -700,8 +730,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (ph == 2) {
           finalize_qkv(p, l, p.ss_in, s_rstd, wtid);
         } else if (ph == 3) {
+          // generic-proxy writes to the region (epilogue staging) before the
+          // TMA writes of the attention operands
+          fence_async_smem();
+          bar128();
           for (int w = cta; w < p.heads * p.nkb; w += G)
-            attention_item(p, l, w, region, wtid, tr && l == 0 && w == cta);
+            attention_item(p, l, w, region, a_full, (a_items++) & 1, &ta_q, &ta_k, &ta_v,
+                           wtid, tr && l == 0 && w == cta);
         } else if (ph == 4) {  // merge; clear the QKV accumulators (read in ph 2)
           merge_partials(p, wtid);
           asm volatile("fence.proxy.async.global;" ::: "memory");

@@ -126,6 +126,25 @@ int make_out_map_dense(CUtensorMap* m, void* ptr, bool f32, int64_t rows,
   return FVB_OK;
 }
 
+// Tensor map over a bf16 [layers, rows, dim] cache, box 64 x 64 x 1 with
+// 128-byte swizzle (rows past `rows` read as zeros).
+int make_cache_map(CUtensorMap* m, const void* ptr, int64_t layers, int64_t rows,
+                   int64_t dim) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return fail(FVB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)dim, (cuuint64_t)rows, (cuuint64_t)layers};
+  cuuint64_t strides[2] = {(cuuint64_t)dim * 2, (cuuint64_t)(rows * dim * 2)};
+  cuuint32_t box[3] = {64, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FVB_ERR_INVALID_ARG, "cache tensor map encode failed (%d)", (int)r);
+  return FVB_OK;
+}
+
 // TMA-store epilogues are on unless FVB_TMA_OUT=0.
 bool tma_out_enabled() {
   static const int v = [] {
@@ -854,7 +873,8 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   if (a->n_layers <= 0 || a->n_layers > 64 || a->n_tok <= 0 || a->n_tok > TOK ||
       a->width % 128 || a->width <= 0 || a->mlp % 64 || a->mlp <= 0 ||
       a->head_dim != 256 || a->heads <= 0 || a->n_prefix < 0 ||
-      (a->n_prefix + a->n_tok + 63) / 64 > MAX_NKB)
+      (a->n_prefix + a->n_tok + 63) / 64 > MAX_NKB ||
+      a->cache_rows < a->n_prefix + a->n_tok)
     return fail(FVB_ERR_INVALID_ARG, "fvb_expert_step: unsupported shape");
   Params& p = out->p;
   p.n_layers = a->n_layers; p.n_tok = a->n_tok; p.width = a->width;
@@ -880,7 +900,7 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   p.qkv_bias = a->qkv_bias; p.gu_bias = a->gu_bias;
   p.o_gate = a->o_gate; p.down_gate = a->down_gate;
   p.eps = a->eps; p.x = a->x;
-  p.kc = (const bf16*)a->k_cache; p.vc = (const bf16*)a->v_cache;
+  p.kc = (bf16*)a->k_cache; p.vc = (bf16*)a->v_cache;
   p.cache_layer = a->cache_rows * a->head_dim;
   p.key_valid = a->key_valid; p.blocks = a->blocks; p.positions = a->positions;
   p.rope_cs = a->rope_cs;
@@ -911,7 +931,6 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   p.qb = (bf16*)take((long long)TOK * a->heads * a->head_dim * 2);
   p.xs = (bf16*)take((long long)TOK * a->width * 2);
   p.hb = (bf16*)take((long long)TOK * a->mlp * 2);
-  p.kvs = (bf16*)take((long long)2 * 128 * a->head_dim * 2);
   p.bar = (unsigned*)take(BAR_WORDS * 4);
   out->bytes = off;
   return FVB_OK;
@@ -953,6 +972,14 @@ extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
                        (long long)a->heads * a->head_dim, TOK);
   if (!r) r = make_map(&bmaps[2], p.hb, TOK, a->mlp, a->mlp, TOK);
   if (r) return r;
+  // attention operands: head columns of the rotated queries, and 64-row
+  // blocks of one layer's cache (3-D so that rows past the cache read zeros)
+  CUtensorMap amaps[3];
+  r = make_map(&amaps[0], p.qb, TOK, (long long)a->heads * a->head_dim,
+               (long long)a->heads * a->head_dim, 64);
+  if (!r) r = make_cache_map(&amaps[1], a->k_cache, a->n_layers, a->cache_rows, a->head_dim);
+  if (!r) r = make_cache_map(&amaps[2], a->v_cache, a->n_layers, a->cache_rows, a->head_dim);
+  if (r) return r;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(expert_step_kernel,
@@ -974,7 +1001,7 @@ extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, expert_step_kernel, maps[0], maps[1],
                                      maps[2], maps[3], bmaps[0], bmaps[1],
-                                     bmaps[2], p);
+                                     bmaps[2], amaps[0], amaps[1], amaps[2], p);
   if (e != cudaSuccess)
     return fail(FVB_ERR_CUDA, "fvb_expert_step: launch failed: %s",
                 cudaGetErrorString(e));

@@ -231,9 +231,13 @@ typedef struct fvb_expert_args {
   const float* down_gate;  /* [L, width] or NULL                             */
   float eps;
   float* x;                /* f32 residual [n_tok, width], updated in place  */
-  const void* k_cache;     /* bf16 [L, cache_rows, head_dim]; rows < n_prefix
-                            * are read (the prefix KV cache)                 */
-  const void* v_cache;
+  void* k_cache;           /* bf16 [L, cache_rows, head_dim]: rows < n_prefix
+                            * are read (the prefix KV cache); rows n_prefix ..
+                            * n_prefix+n_tok-1 are written with the step's
+                            * rotated suffix keys / values, as the reference's
+                            * decoder writes them (pi05_flowmatching_inference
+                            * .py:199-210); cache_rows >= n_prefix + n_tok    */
+  void* v_cache;
   int64_t cache_rows;
   const uint8_t* key_valid;  /* [n_prefix] or NULL                          */
   const int32_t* blocks;     /* [n_tok] suffix attention block ids (cumsum

@@ -212,8 +212,11 @@ def expert_step(a):
         r = torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1)
         q, k = r[:, :H], r[:, H]
         v = acc[:, (H + 1) * hd:]
-        kk = torch.cat([a.k_cache[l, :E].float(), k.bfloat16().float()])
-        vv = torch.cat([a.v_cache[l, :E].float(), v.bfloat16().float()])
+        # the suffix keys / values land in the cache rows after the prefix
+        a.k_cache[l, E:E + S] = k.bfloat16()
+        a.v_cache[l, E:E + S] = v.bfloat16()
+        kk = a.k_cache[l, :E + S].float()
+        vv = a.v_cache[l, :E + S].float()
         mask = torch.ones(S, E + S, dtype=torch.bool)
         if a.key_valid is not None:
             mask[:, :E] &= a.key_valid[:E].bool()[None]
