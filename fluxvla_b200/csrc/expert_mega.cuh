@@ -646,6 +646,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const CUtensorMap* maps[N_GEMM] = {&tm_qkv, &tm_o, &tm_gu, &tm_down};
+  // programmatic dependent launch: the next kernel may be scheduled now (it
+  // waits for this grid's completion before touching its outputs); the
+  // weight producer streams static weights at once, everything that reads
+  // activations waits for the previous kernel first
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ---- weight producer: every tile of every GEMM item, in order ----
@@ -705,6 +710,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---- workers: B builders, epilogues, attention, merges, barriers ----
+    griddep_wait();
     const int wtid = threadIdx.x - 64;
     const int q = warp & 3;
     // epilogue transpose stage: [4 warps][16 tokens][32 features + 4]

@@ -994,14 +994,28 @@ extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeCooperative;
   attrs[0].val.cooperative = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  // the weight stream of the step starts under the previous kernel's tail
+  // when the driver accepts a cooperative launch with programmatic
+  // serialisation; otherwise the plain cooperative launch
+  static int coop_pdl = -1;
+  if (coop_pdl < 0) coop_pdl = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = coop_pdl ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, expert_step_kernel, maps[0], maps[1],
                                      maps[2], maps[3], bmaps[0], bmaps[1],
                                      bmaps[2], amaps[0], amaps[1], amaps[2], p);
+  if (e != cudaSuccess && coop_pdl) {
+    cudaGetLastError();
+    coop_pdl = 0;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, expert_step_kernel, maps[0], maps[1], maps[2], maps[3],
+                           bmaps[0], bmaps[1], bmaps[2], amaps[0], amaps[1], amaps[2], p);
+  }
   if (e != cudaSuccess)
     return fail(FVB_ERR_CUDA, "fvb_expert_step: launch failed: %s",
                 cudaGetErrorString(e));
