@@ -35,3 +35,10 @@ def test_signature_matches_reference(name):
         else:
             assert p.default is inspect.Parameter.empty, p.name
     assert f'{ref_file}:{SIGS[name]["line"]}' in fn.__doc__
+
+
+def test_triton_style_launchers_need_a_grid():
+    k = attention_triton_ops.matmul_abT_scale
+    assert k[(1,)] is k[(148, 1, 1)]  # the grid is a tuning knob, ignored
+    with pytest.raises(TypeError):
+        k(None, None, None, 1, 1, 1, 1.0)
