@@ -2,16 +2,23 @@
 // flow-matching step (action-expert Gemma stack over <= 64 suffix tokens) in
 // one cooperative launch, one CTA per SM.
 //
-// Per layer, six phases separated by grid barriers:
-//   P1 QKV   acc_qkv[t,f] += W_qkv[f,k] * (x[t,k](1+w_in[k]))  (split-K, f32
-//            atomics); the row-tile-0 items also add sum_k x^2 into ss_in[t]
-//   P2 ATT   per (head, 64-key block): q,k,v = rope(rstd_in[t]*acc + bias),
-//            masked attention over prefix cache keys + suffix keys -> partial
-//   P3 CMB   merge the key-block partials -> attn[t, h*hd + d] (bf16)
-//   P4 O     x[t,f] += gate_o[f] * (W_o attn)  (split-K atomics)
-//   P5 GU    acc_gu[t,f] += W_gu[f,k] * (x[t,k](1+w_post[k])), ss_post[t]
-//   P6 DOWN  x[t,f] += gate_d[f] * (W_down gelu(g)*u), with
-//            g,u = rstd_post[t]*acc_gu + bias built into the MMA's B operand
+// Per layer, ten phases separated by grid barriers:
+//   0 prep    xs[t,k] = bf16(x[t,k](1+w_in[k])), ss_in[t] += sum_k x^2
+//   1 QKV     acc_qkv[t,f] += W_qkv[f,k] xs[t,k]  (split-K, f32 reductions;
+//             B operand = xs by TMA)
+//   2 finalize q,k,v = rope(rstd_in[t]*acc + bias) as bf16: q to qb, the
+//             suffix k / v into the layer's cache rows n_prefix..
+//   3 ATT     per (head, 64-key block): Q, K, V tiles by TMA, masked
+//             attention over prefix + suffix keys -> bf16 partial, (max, sum)
+//   4 merge   key-block partials -> attn[t, h*hd + d] (bf16)
+//   5 O       x[t,f] += gate_o[f] * (W_o attn)  (split-K reductions)
+//   6 prep    xs = bf16(x(1+w_post)), ss_post
+//   7 GU      acc_gu[t,f] += W_gu[f,k] xs[t,k]
+//   8 GeGLU   hb[t,i] = bf16(gelu(rs*g + bg) * (rs*u + bu)), rs = rstd_post
+//   9 DOWN    x[t,f] += gate_d[f] * (W_down hb)
+// Each phase costs about one L2 round trip plus one grid barrier; folding a
+// reshaping phase into its consumer was measured slower (every consumer CTA
+// then re-reads the f32 activations of its K slice).
 // RMSNorm is linear in the un-normalised row apart from the per-token factor
 // rstd, so the GEMM runs on x*(1+w) and rstd is applied by the consumer; for
 // adaRMSNorm the shift enters as W*shift, precomputed per step (bias arrays).
@@ -20,9 +27,9 @@
 // STAGES-deep TMA ring in a fixed order and never waits for a barrier (the
 // weights do not depend on the previous phase); warp 1 lane 0 issues
 // tcgen05.mma (M=128 weight rows, N=64 tokens, K=16) into a 64-column TMEM
-// accumulator; warps 2..5 build the B operand (tokens x K-slice, bf16, 128-byte
-// swizzle) in shared memory, run the epilogue atomics, the attention and the
-// merge, and take part in the grid barriers.
+// accumulator; warps 2..5 issue the B operand TMA (tokens x K-slice, bf16,
+// 128-byte swizzle), run the epilogue reductions, the prep / finalize /
+// merge phases and the attention, and take part in the grid barriers.
 #pragma once
 
 #include "attention.cuh"
