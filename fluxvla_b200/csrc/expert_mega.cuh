@@ -98,7 +98,7 @@ struct Params {
 };
 
 // Diagnostics: per CTA, globaltimer at worker start, then after the work
-// and after the barrier of each of the 6 phases of layer 0.
+// and after the barrier of each of the 10 phases of layer 0 (slots 24.. hold stamps inside the attention phase).
 __device__ unsigned long long g_mega_trace[256][32];
 
 // ---------------------------------------------------------------------------
