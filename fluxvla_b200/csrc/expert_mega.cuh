@@ -647,11 +647,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tensormap(&ta_k);
     prefetch_tensormap(&ta_v);
   }
+  // An abort flag left raised by an earlier launch on this workspace (one of
+  // whose waits gave up) is reported, and the launch then does no work at
+  // all (no copy or MMA is issued) instead of returning silently wrong
+  // results; the host clears the workspace after reading the status.
+  __shared__ int s_skip;
+  if (threadIdx.x == 0) {
+    s_skip = aborted(p) ? 1 : 0;
+    if (s_skip && cta == 0) record_device_error(FVB_ERR_DEVICE_TIMEOUT);
+  }
   if (warp == 1) tmem_alloc(tmem_slot, 64);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const bool skip = s_skip != 0;
   const CUtensorMap* maps[N_GEMM] = {&tm_qkv, &tm_o, &tm_gu, &tm_down};
   // programmatic dependent launch: the next kernel may be scheduled now (it
   // waits for this grid's completion before touching its outputs); the
@@ -659,7 +669,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // activations waits for the previous kernel first
   griddep_launch_dependents();
 
-  if (warp == 0) {
+  if (skip) {
+    // nothing issued: straight to the TMEM release
+  } else if (warp == 0) {
     // ---- weight producer: every tile of every GEMM item, in order ----
     if (lane == 0) {
       const uint64_t pol = l2_evict_first_policy();

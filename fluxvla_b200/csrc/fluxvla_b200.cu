@@ -6,6 +6,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "attention.cuh"
 #include "attention_tc.cuh"
@@ -198,19 +200,33 @@ int sm_count() {
   return counts[dev];
 }
 
+
+// cudaFuncSetAttribute applies to the current device only, so the raised
+// dynamic shared memory limit is remembered per (kernel, device): a process
+// that drives several GPUs through this library sets it on each of them.
+int ensure_smem(const void* kern, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({kern, dev})) return FVB_OK;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "%s: shared memory attribute: %s", what,
+                cudaGetErrorString(e));
+  done.insert({kern, dev});
+  return FVB_OK;
+}
+
 template <int BN, int EPI, bool SWAP, int ACT = FVB_ACT_NONE>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb,
                 const CUtensorMap& mo, const fvb::GemmDev& d, cudaStream_t st) {
   using C = fvb::GemmCfg<BN>;
   auto kern = fvb::gemm_tc_kernel<BN, C::STAGES, EPI, SWAP, ACT>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess)
-      return fail(FVB_ERR_CUDA, "gemm smem attribute: %s",
-                  cudaGetErrorString(cudaGetLastError()));
-    attr = true;
-  }
+  if (int rr = ensure_smem(reinterpret_cast<const void*>(kern), C::SMEM, "gemm")) return rr;
   const int grid = d.n_work < sm_count() ? d.n_work : sm_count();
   return launch_k("fvb_gemm", kern, dim3(grid), dim3(fvb::GEMM_THREADS),
                   (size_t)C::SMEM, st, ma, mb, mo, d);
@@ -223,14 +239,7 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb,
                      const CUtensorMap& mo, const fvb::GemmDev& d, cudaStream_t st) {
   using C = fvb::pair::PairCfg<BN>;
   auto kern = fvb::pair::gemm_pair_kernel<BN, EPI>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess)
-      return fail(FVB_ERR_CUDA, "gemm pair smem attribute: %s",
-                  cudaGetErrorString(cudaGetLastError()));
-    attr = true;
-  }
+  if (int rr = ensure_smem(reinterpret_cast<const void*>(kern), C::SMEM, "gemm pair")) return rr;
   const int pairs_max = sm_count() / 2;
   const int pairs = d.n_work < pairs_max ? d.n_work : pairs_max;
   cudaLaunchConfig_t cfg = {};
@@ -336,14 +345,7 @@ int launch_attn_tc(const fvb_attn_args* a, const fvb::AttnDev& d,
   p.trace = g_trace_next;
   g_trace_next = 0;
   auto kern = A::attn_tc_kernel<HD, HDP, NV>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess)
-      return fail(FVB_ERR_CUDA, "attention smem attribute: %s",
-                  cudaGetErrorString(cudaGetLastError()));
-    attr = true;
-  }
+  if (int rr = ensure_smem(reinterpret_cast<const void*>(kern), C::SMEM, "attention")) return rr;
   const int tiles = (a->group * a->n_q + A::BM - 1) / A::BM;
   return launch_k("fvb_attention", kern,
                   dim3(tiles, a->heads / a->group, a->batch * d.splits),
@@ -675,22 +677,12 @@ int fvb_attention(const fvb_attn_args* a, void* stream) {
             a->batch * d.splits);
   if (a->head_dim == 256) {
     constexpr int S = fvb::attn_smem_bytes<256, 256>();
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(fvb::attn_kernel<256, 256>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, S);
-      attr = true;
-    }
+    if (int rr = ensure_smem(reinterpret_cast<const void*>(fvb::attn_kernel<256, 256>), S, "fvb_attention")) return rr;
     return launch_k("fvb_attention", fvb::attn_kernel<256, 256>, grid,
                     dim3(fvb::ATT_THREADS), (size_t)S, st, d);
   } else {
     constexpr int S = fvb::attn_smem_bytes<72, 80>();
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(fvb::attn_kernel<72, 80>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, S);
-      attr = true;
-    }
+    if (int rr = ensure_smem(reinterpret_cast<const void*>(fvb::attn_kernel<72, 80>), S, "fvb_attention")) return rr;
     return launch_k("fvb_attention", fvb::attn_kernel<72, 80>, grid,
                     dim3(fvb::ATT_THREADS), (size_t)S, st, d);
   }
@@ -980,15 +972,7 @@ extern "C" int fvb_expert_step(const fvb_expert_args* a, void* stream) {
   if (!r) r = make_cache_map(&amaps[1], a->k_cache, a->n_layers, a->cache_rows, a->head_dim);
   if (!r) r = make_cache_map(&amaps[2], a->v_cache, a->n_layers, a->cache_rows, a->head_dim);
   if (r) return r;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(expert_step_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
-      return fail(FVB_ERR_CUDA, "expert smem attribute: %s",
-                  cudaGetErrorString(cudaGetLastError()));
-    attr = true;
-  }
+  if (int rr = ensure_smem(reinterpret_cast<const void*>(expert_step_kernel), SMEM_BYTES, "expert")) return rr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sm_count());
   cfg.blockDim = dim3(THREADS);
@@ -1043,10 +1027,34 @@ static __device__ __align__(256) unsigned char
 
 // Device address of g_noalloc_scratch for the current device.  In host code
 // the symbol name is only a host-side stand-in, so the address is looked up
-// once per device (with that device current) and cached.
+// with cudaGetSymbolAddress (with that device current) on the first call on
+// each device and cached together with the CUDA context it belongs to.  A
+// cudaDeviceReset destroys that context and reloads the module, so a call
+// that finds a different current context looks the address up again instead
+// of reusing a stale pointer.  The first call on a device should come before
+// any stream capture.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
 static int noalloc_scratch(void** out) {
   static std::mutex mu;
   static void* ptrs[128] = {};
+  static CUcontext ctxs[128] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess)
@@ -1054,8 +1062,15 @@ static int noalloc_scratch(void** out) {
                 cudaGetErrorString(e));
   if (dev < 0 || dev >= 128)
     return fail(FVB_ERR_UNSUPPORTED, "fvb_attention_noalloc: device %d", dev);
+  // a runtime call on the device binds its primary context before the
+  // context handle is read
+  int n_sm = 0;
+  e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess)
+    return fail(FVB_ERR_CUDA, "fvb_attention_noalloc: %s", cudaGetErrorString(e));
+  const CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lk(mu);
-  if (!ptrs[dev]) {
+  if (!ptrs[dev] || ctxs[dev] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p)
@@ -1063,6 +1078,7 @@ static int noalloc_scratch(void** out) {
                   "fvb_attention_noalloc: cudaGetSymbolAddress: %s",
                   cudaGetErrorString(e));
     ptrs[dev] = p;
+    ctxs[dev] = ctx;
   }
   *out = ptrs[dev];
   return FVB_OK;
@@ -1094,13 +1110,15 @@ extern "C" int fvb_attention_noalloc(const fvb_attn_args* a, void* stream) {
             a->batch * d.splits);
   if (a->head_dim == 256) {
     constexpr int S = fvb::attn_smem_bytes<256, 256>();
-    cudaFuncSetAttribute(fvb::attn_kernel<256, 256>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, S);
+    r = ensure_smem(reinterpret_cast<const void*>(fvb::attn_kernel<256, 256>), S,
+                    "fvb_attention_noalloc");
+    if (r) return r;
     fvb::attn_kernel<256, 256><<<grid, fvb::ATT_THREADS, S, st>>>(d);
   } else {
     constexpr int S = fvb::attn_smem_bytes<72, 80>();
-    cudaFuncSetAttribute(fvb::attn_kernel<72, 80>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, S);
+    r = ensure_smem(reinterpret_cast<const void*>(fvb::attn_kernel<72, 80>), S,
+                    "fvb_attention_noalloc");
+    if (r) return r;
     fvb::attn_kernel<72, 80><<<grid, fvb::ATT_THREADS, S, st>>>(d);
   }
   r = check_launch("fvb_attention_noalloc");

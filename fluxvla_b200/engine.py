@@ -654,4 +654,31 @@ class PI0EngineB200:
                                        pin_memory=True)
         self._x_host.copy_(self.B['x_t'], non_blocking=True)
         torch.cuda.current_stream(self.dev).synchronize()
+        self.check_device_status()
         return self._x_host.clone().reshape(1, self.A, -1)
+
+    def check_device_status(self):
+        """Raise if a kernel of the last replay gave up a bounded wait.
+
+        The kernels never trap: a wait that runs past its limit records
+        FVB_ERR_DEVICE_TIMEOUT in the library's status word and returns, so
+        that chunk's actions are invalid.  The status word is read after the
+        chunk's synchronisation; on an error it is cleared, the engine's
+        synchronisation state (the persistent step's barrier counter and
+        abort flag, split-K workspaces) is zeroed so that the next chunk
+        starts clean, and the error is raised."""
+        st = ops.device_status()
+        if st:
+            ops.device_status(reset=True)
+            self.reset_sync_state()
+            raise RuntimeError(
+                f'fluxvla_b200: device status {st} (a kernel wait gave up); '
+                'the actions of this chunk are invalid, the engine has been '
+                'reset for the next call')
+
+    def reset_sync_state(self):
+        """Zero every workspace that carries state between launches."""
+        for k in ('expert_ws', 'gemm_ws', 'norm_sync', 'prefix_attn_ws'):
+            if k in self.B:
+                self.B[k].zero_()
+        torch.cuda.synchronize(self.dev)

@@ -15,6 +15,18 @@
  *
  * Each entry point names the reference interface it replaces
  * (paths relative to the FluxVLA project root).
+ *
+ * Environment switches read by the library (diagnostics and A/B
+ * measurements; none changes results beyond float rounding order, and the
+ * defaults are the production path):
+ *   FVB_PDL=0            launch without programmatic dependent launch
+ *   FVB_TMA_OUT=0        GEMM epilogues write back per row instead of TMA
+ *   FVB_ATTN_TC=0        prefill attention on the mma.sync kernel instead
+ *                        of the tcgen05 kernel
+ *   FVB_EXPERT_STAGES=n  weight-ring depth of fvb_expert_step (1..6)
+ *   FVB_EXPERT_TRACE=1   fvb_expert_step records per-phase timestamps
+ *                        (read with fvb_expert_trace_read)
+ * The trace entry points at the end of this header are diagnostics only.
  */
 #ifndef FLUXVLA_B200_H_
 #define FLUXVLA_B200_H_

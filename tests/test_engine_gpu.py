@@ -105,3 +105,53 @@ def test_full_pi0_config2_full_depth():
     out = eng.predict_action(imgs, toks, state, noise=noise)
     ref = O.predict_action(cfg, W, imgs, toks, state, noise)
     check_actions(out, ref)
+
+
+@pytest.mark.slow
+def test_full_pi05_config3_full_depth():
+    """config[3]: full PI0.5 (27 SigLIP + 18 Gemma + 18 adaRMS expert layers,
+    848-row prefix = 3 views + 48 text + 32 state tokens, 50 action tokens)."""
+    cfg = pi05_config()
+    W = make_weights(cfg, 9)
+    imgs, toks, state, noise = request(cfg, 10, 80)
+    eng = PI0EngineB200(cfg, W, prefix_len=848)
+    out = eng.predict_action(imgs, toks, state, noise=noise)
+    ref = O.predict_action(cfg, W, imgs, toks, state, noise)
+    check_actions(out, ref)
+
+
+def _abort_word(eng):
+    """The persistent step's abort flag inside the engine's workspace: the
+    barrier block (320 words, 256-byte aligned) is the workspace's last
+    piece and the flag is its word 288."""
+    ws = eng.B['expert_ws']
+    bar_bytes = (320 * 4 + 255) // 256 * 256
+    off = ws.numel() - bar_bytes + 288 * 4
+    return ws[off:off + 4]
+
+
+def test_stale_abort_flag_is_reported_and_cleared():
+    """Failure detection without a GPU fault: the abort flag a timed-out wait
+    would leave behind is raised from the host; the next chunk must report
+    FVB_ERR_DEVICE_TIMEOUT through predict_action (not return silent
+    garbage), and the chunk after that must be clean again."""
+    from fluxvla_b200 import ops
+    cfg = PI0Config(exp_layers=2, llm_layers=2)
+    W = make_weights(cfg, 1, parts=('exp', 'heads'))
+    E = 816
+    g = torch.Generator().manual_seed(3)
+    k = torch.randn(cfg.exp_layers, E, cfg.head_dim, generator=g).bfloat16()
+    v = torch.randn(cfg.exp_layers, E, cfg.head_dim, generator=g).bfloat16()
+    state = torch.randn(1, cfg.state_dim, generator=g)
+    noise = torch.randn(1, cfg.n_actions, cfg.action_dim, generator=g)
+    eng = PI0EngineB200(cfg, W, prefix_len=E)
+    eng.set_prefix_cache(k.cuda(), v.cuda())
+    ops.device_status(reset=True)
+    clean = eng.predict_action(states=state, noise=noise)
+    assert torch.isfinite(clean).all()
+    _abort_word(eng).fill_(1)
+    with pytest.raises(RuntimeError, match='device status 4'):
+        eng.predict_action(states=state, noise=noise)
+    assert ops.device_status() == 0
+    again = eng.predict_action(states=state, noise=noise)
+    assert (again - clean).abs().max().item() < 1e-2

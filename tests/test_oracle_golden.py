@@ -75,3 +75,34 @@ def test_resize_matches_opencv_golden():
     for (seed, h, w, H, W) in d['cases']:
         got = resize_linear_u8(source(seed, h, w), H, W)
         assert torch.equal(torch.from_numpy(got), d['outputs'][(seed, h, w, H, W)]), (h, w, H, W)
+
+
+def _predict_real_width(name, atol):
+    d = _load(name)
+    cfg = PI0Config(**d['cfg'])
+    W = make_weights(cfg, d['seed'])
+    out = _predict(d)
+    torch.testing.assert_close(out, d['actions'], atol=atol, rtol=1e-4)
+    V = cfg.n_views
+    pix = O.normalize_images(d['images'], [cfg.img_mean] * V,
+                             [cfg.img_std] * V).reshape(1, 3 * V,
+                                                        cfg.image_size,
+                                                        cfg.image_size)
+    embs, _, _ = O.embed_prefix(cfg, W, pix, d['lang_tokens'],
+                                torch.ones(1, V, dtype=torch.bool),
+                                d['lang_masks'])
+    torch.testing.assert_close(embs[:, d['prefix_rows']], d['prefix_embs'],
+                               atol=1e-4, rtol=1e-4)
+
+
+def test_pi0_real_width_matches_reference():
+    """Production widths (SigLIP 1152/hd 72 on a 256-token view, Gemma-2B
+    layer over 272 prefix rows, expert layer 1024 wide, 51 suffix rows):
+    prefix embeddings and the 10-step actions of the reference's own eager
+    PI0FlowMatching.predict_action."""
+    _predict_real_width('pi0_real_width.pt', 1e-4)
+
+
+def test_pi05_real_width_matches_reference():
+    """As above for PI05FlowMatching (adaRMS expert, 304 prefix rows)."""
+    _predict_real_width('pi05_real_width.pt', 1e-4)
