@@ -133,26 +133,55 @@ def _read_one(path: str, keys: Optional[set] = None) -> Dict[str, torch.Tensor]:
     return out
 
 
-def read_safetensors(path: str, keys: Optional[Iterable[str]] = None
-                     ) -> Dict[str, torch.Tensor]:
-    """Tensors of a .safetensors file, or of every shard listed by a
-    `*.safetensors.index.json` (its weight_map), or of the checkpoint in a
-    directory (model.safetensors or model.safetensors.index.json).
-    `keys` restricts the result (and the bytes read) to those names."""
-    want = None if keys is None else set(keys)
+def _header(path: str) -> dict:
+    with open(path, 'rb') as f:
+        (n,) = struct.unpack('<Q', f.read(8))
+        return json.loads(f.read(n))
+
+
+def safetensors_index(path: str) -> Dict[str, str]:
+    """tensor name -> file holding it, for a .safetensors file, a
+    `*.safetensors.index.json` (its weight_map) or a directory (its
+    model.safetensors.index.json, its model.safetensors, or else every
+    .safetensors file in it, as BaseVLA.from_pretrained reads a directory,
+    base_vla.py:199-207).  Only headers are read."""
     if os.path.isdir(path):
         idx = os.path.join(path, 'model.safetensors.index.json')
-        path = idx if os.path.exists(idx) else os.path.join(path, 'model.safetensors')
+        one = os.path.join(path, 'model.safetensors')
+        if os.path.exists(idx):
+            path = idx
+        elif os.path.exists(one):
+            path = one
+        else:
+            out = {}
+            for fn in sorted(os.listdir(path)):
+                if fn.endswith('.safetensors'):
+                    fp = os.path.join(path, fn)
+                    out.update({k: fp for k in _header(fp)
+                                if k != '__metadata__'})
+            return out
     if path.endswith('.json'):
         with open(path) as f:
             wmap = json.load(f)['weight_map']
         root = os.path.dirname(path)
-        files = sorted({fn for k, fn in wmap.items() if want is None or k in want})
-        out = {}
-        for fn in files:
-            out.update(_read_one(os.path.join(root, fn), want))
-        return out
-    return _read_one(path, want)
+        return {k: os.path.join(root, fn) for k, fn in wmap.items()}
+    return {k: path for k in _header(path) if k != '__metadata__'}
+
+
+def read_safetensors(path: str, keys: Optional[Iterable[str]] = None
+                     ) -> Dict[str, torch.Tensor]:
+    """Tensors of a .safetensors file, of every shard listed by a
+    `*.safetensors.index.json`, or of the checkpoint in a directory (see
+    safetensors_index).  `keys` restricts the result (and the bytes read) to
+    those names."""
+    want = None if keys is None else set(keys)
+    index = safetensors_index(path)
+    files = sorted({fn for k, fn in index.items()
+                    if want is None or k in want})
+    out = {}
+    for fn in files:
+        out.update(_read_one(fn, want))
+    return out
 
 
 def write_safetensors(path: str, tensors: Dict[str, torch.Tensor]) -> None:
@@ -207,11 +236,124 @@ def weights_from_state_dict(sd: Dict[str, torch.Tensor], cfg: PI0Config,
     return out
 
 
+# The reference configs' checkpoint name mappings for openpi checkpoints
+# (configs/pi0/pi0_paligemma_libero_10_full_finetune.py:106-118 and
+# configs/pi05/pi05_paligemma_aloha+ur_4090_full_finetune.py:104-116): a
+# substring of the model's parameter name -> its replacement in the
+# checkpoint.  The entries are data that must equal the reference's to read
+# the same files.
+PI0_NAME_MAPPING = {
+    'llm_backbone': 'paligemma_with_expert.paligemma.model.language_model',
+    'vision_backbone.vision':
+    'paligemma_with_expert.paligemma.model.vision_tower',
+    'projector.projector':
+    'paligemma_with_expert.paligemma.model.multi_modal_projector.linear',
+    'llm_expert': 'paligemma_with_expert.gemma_expert.model',
+    'action_time_mlp_in.projector': 'action_time_mlp_in',
+    'action_time_mlp_out.projector': 'action_time_mlp_out',
+    'state_proj.projector': 'state_proj',
+    'action_in_proj.projector': 'action_in_proj',
+    'action_out_proj.projector': 'action_out_proj',
+    'llm_backbone.embed_tokens': 'paligemma_with_expert.paligemma.lm_head',
+}
+PI05_NAME_MAPPING = {
+    k: v for k, v in PI0_NAME_MAPPING.items()
+    if not k.startswith(('action_time_mlp', 'state_proj'))}
+PI05_NAME_MAPPING.update({'time_mlp_in.projector': 'time_mlp_in',
+                          'time_mlp_out.projector': 'time_mlp_out'})
+
+
+def default_name_mapping(cfg: PI0Config) -> Dict[str, str]:
+    return dict(PI05_NAME_MAPPING if cfg.adarms else PI0_NAME_MAPPING)
+
+
+def mapped_key(model_name: str, name_mapping: Dict[str, str],
+               available) -> Optional[str]:
+    """The checkpoint key of one model parameter under a substring mapping,
+    following BaseVLA.from_pretrained (base_vla.py:226-262): every mapping
+    entry whose key occurs in the name proposes name.replace(key, value);
+    the proposal present in the checkpoint wins; two present proposals are
+    an error; none is a miss (None)."""
+    hit = None
+    for key, val in name_mapping.items():
+        if key in model_name:
+            cand = model_name.replace(key, val)
+            if cand not in available:
+                continue
+            if hit is not None and hit != cand:
+                raise ValueError(f"parameter '{model_name}' matched several "
+                                 f"checkpoint keys: '{hit}', '{cand}'")
+            hit = cand
+    return hit
+
+
+def read_checkpoint(path: str, keys: Optional[Iterable[str]] = None
+                    ) -> Dict[str, torch.Tensor]:
+    """Tensors of a checkpoint: safetensors file / sharded index /
+    directory of .safetensors files, or a torch .pt / .pth file holding a
+    state dict or {'model': state dict} (base_vla.py:190-222)."""
+    if path.endswith(('.pt', '.pth')):
+        ck = torch.load(path, map_location='cpu', weights_only=True)
+        if isinstance(ck, dict) and 'model' in ck and isinstance(
+                ck['model'], dict):
+            ck = ck['model']
+        if not isinstance(ck, dict):
+            raise ValueError(f'{path}: not a state dict')
+        if keys is not None:
+            ks = set(keys)
+            ck = {k: v for k, v in ck.items() if k in ks}
+        return ck
+    if path.endswith('.safetensors') or os.path.isdir(path) or \
+            path.endswith('.json'):
+        return read_safetensors(path, keys)
+    raise ValueError(f'unsupported checkpoint format: {path}')
+
+
+def checkpoint_keys(path: str) -> set:
+    """Names of every tensor in a checkpoint (reads headers only for
+    safetensors)."""
+    if path.endswith(('.pt', '.pth')):
+        return set(read_checkpoint(path).keys())
+    return set(safetensors_index(path).keys())
+
+
 def load_pretrained(path: str, cfg: PI0Config,
                     parts: Iterable[str] = ('vision', 'llm', 'exp', 'heads'),
-                    strip_prefix: str = '', device='cpu') -> Dict[str, torch.Tensor]:
-    """Checkpoint file / index / directory -> weights for PI0EngineB200."""
+                    strip_prefix: str = '', device='cpu',
+                    name_mapping: Optional[Dict[str, str]] = None
+                    ) -> Dict[str, torch.Tensor]:
+    """Checkpoint (safetensors file / index / directory, or .pt / .pth) ->
+    weights for PI0EngineB200.
+
+    Without ``name_mapping`` the checkpoint carries the reference model's own
+    state_dict names (optionally under ``strip_prefix``).  With one (e.g.
+    ``default_name_mapping(cfg)`` for openpi ``pi0_base`` / ``pi05_base``
+    checkpoints) each model name is translated as the reference's
+    ``from_pretrained`` does; ``name_mapping='auto'`` picks the config's
+    default mapping when the checkpoint uses openpi names."""
     nm = reference_name_map(cfg)
-    keys = [strip_prefix + nm[n] for n, _, _ in weight_shapes(cfg, parts)]
-    sd = read_safetensors(path, keys)
-    return weights_from_state_dict(sd, cfg, parts, strip_prefix, device)
+    names = [n for n, _, _ in weight_shapes(cfg, parts)]
+    if name_mapping == 'auto':
+        avail = checkpoint_keys(path)
+        direct = sum((strip_prefix + nm[n]) in avail for n in names)
+        name_mapping = None if direct == len(names) else \
+            default_name_mapping(cfg)
+    if not name_mapping:
+        keys = [strip_prefix + nm[n] for n in names]
+        sd = read_checkpoint(path, keys)
+        return weights_from_state_dict(sd, cfg, parts, strip_prefix, device)
+    avail = checkpoint_keys(path)
+    want, missing = {}, []
+    for n in names:
+        k = mapped_key(nm[n], name_mapping, avail)
+        if k is None:
+            missing.append(nm[n])
+        else:
+            want[nm[n]] = k
+    if missing:
+        raise KeyError(f'{len(missing)} parameters not found in the '
+                       f'checkpoint under the name mapping: {missing[:8]}'
+                       f'{" ..." if len(missing) > 8 else ""}')
+    raw = read_checkpoint(path, set(want.values()))
+    sd = {ours: raw[theirs] for ours, theirs in want.items()}
+    return weights_from_state_dict(sd, cfg, parts, '', device)

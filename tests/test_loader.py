@@ -95,3 +95,76 @@ def test_missing_and_mismatched_tensors():
     sd[nm['proj_w']] = torch.zeros(3, 3)
     with pytest.raises(ValueError, match='projector'):
         weights_from_state_dict(sd, cfg)
+
+
+def _openpi_state_dict(cfg, W, dtype=torch.float32):
+    """The reference state dict renamed as an openpi checkpoint stores it
+    (the inverse of the config's name_mapping), with the token embedding
+    under the lm_head name only."""
+    from fluxvla_b200.loader import default_name_mapping
+    nm = reference_name_map(cfg)
+    mp = default_name_mapping(cfg)
+    sd = {}
+    for ours, theirs in nm.items():
+        if ours not in W:
+            continue
+        if theirs == 'llm_backbone.embed_tokens.weight':
+            key = 'paligemma_with_expert.paligemma.lm_head.weight'
+        else:
+            key = theirs
+            for k in sorted(mp, key=len, reverse=True):
+                if k in theirs and k != 'llm_backbone.embed_tokens':
+                    key = theirs.replace(k, mp[k])
+                    break
+        sd[key] = W[ours].to(dtype)
+    return sd
+
+
+@pytest.mark.parametrize('pi05', [False, True])
+def test_openpi_names_through_name_mapping(tmp_path, pi05):
+    cfg = tiny(pi05)
+    W = make_weights(cfg, seed=5)
+    sd = _openpi_state_dict(cfg, W)
+    assert any(k.startswith('paligemma_with_expert.gemma_expert.model.')
+               for k in sd)
+    path = str(tmp_path / 'model.safetensors')
+    write_safetensors(path, sd)
+    from fluxvla_b200.loader import default_name_mapping
+    for mapping in (default_name_mapping(cfg), 'auto'):
+        got = load_pretrained(path, cfg, name_mapping=mapping)
+        assert set(got) == set(W)
+        for k in W:
+            assert torch.equal(got[k], W[k].bfloat16()), k
+    with pytest.raises(KeyError):
+        load_pretrained(path, cfg)  # the model's own names are absent
+
+
+@pytest.mark.parametrize('wrap', [False, True])
+def test_torch_pt_checkpoint(tmp_path, wrap):
+    cfg = tiny()
+    W = make_weights(cfg, seed=6)
+    sd = reference_state_dict(cfg, W)
+    path = str(tmp_path / 'ckpt.pth')
+    torch.save({'model': sd, 'step': 3} if wrap else sd, path)
+    got = load_pretrained(path, cfg)
+    for k in W:
+        assert torch.equal(got[k], W[k].bfloat16()), k
+    from fluxvla_b200.loader import default_name_mapping
+    path2 = str(tmp_path / 'openpi.pt')
+    torch.save(_openpi_state_dict(cfg, W), path2)
+    got = load_pretrained(path2, cfg, name_mapping=default_name_mapping(cfg))
+    assert torch.equal(got['exp.l0.q_w'], W['exp.l0.q_w'].bfloat16())
+
+
+def test_directory_of_unindexed_shards(tmp_path):
+    cfg = tiny()
+    W = make_weights(cfg, seed=7)
+    sd = reference_state_dict(cfg, W)
+    ks = sorted(sd)
+    write_safetensors(str(tmp_path / 'a.safetensors'),
+                      {k: sd[k] for k in ks[::2]})
+    write_safetensors(str(tmp_path / 'b.safetensors'),
+                      {k: sd[k] for k in ks[1::2]})
+    got = load_pretrained(str(tmp_path), cfg)
+    for k in W:
+        assert torch.equal(got[k], W[k].bfloat16()), k
