@@ -101,6 +101,8 @@ EXPORTS = {
                                       C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_int64, C.c_void_p]),
     'fvb_probe_wait_timeout': (C.c_int, [C.c_int64, C.c_void_p, C.c_void_p]),
+    'fvb_patchify_f32': (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
+                                   C.c_int32, C.c_void_p, C.c_int64, C.c_void_p]),
     'fvb_patchify': (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                C.c_int32, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_int64, C.c_void_p]),

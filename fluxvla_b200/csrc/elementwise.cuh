@@ -222,6 +222,31 @@ __global__ void patchify_kernel(const uint8_t* __restrict__ img, int H, int W,
   }
 }
 
+// Normalised float CHW pixels [views, 3, H, W] (the reference model's
+// `images` input after its NormalizeImages transform) -> bf16 patch rows in
+// the layout of patchify_kernel.  One CTA per patch row; a warp reads 32
+// consecutive x of one (channel, ky) line of the patch.
+__global__ void patchify_f32_kernel(const float* __restrict__ pix, int H, int W,
+                                    int P, bf16* __restrict__ out,
+                                    long long ldo) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int gw = W / P, gh = H / P;
+  const int r = blockIdx.x;
+  const int v = r / (gh * gw), py = (r / gw) % gh, px = r % gw;
+  const int K = 3 * P * P;
+  bf16* o = out + (long long)r * ldo;
+  for (int col = threadIdx.x; col < ldo; col += blockDim.x) {
+    float val = 0.f;
+    if (col < K) {
+      const int c = col / (P * P), ky = (col / P) % P, kx = col % P;
+      const int y = py * P + ky, x = px * P + kx;
+      val = __ldg(pix + (((long long)v * 3 + c) * H + y) * W + x);
+    }
+    o[col] = __float2bfloat16(val);
+  }
+}
+
 __global__ void embed_kernel(const long long* __restrict__ ids,
                              const bf16* __restrict__ table, int dim,
                              float scale, float* __restrict__ out,

@@ -791,6 +791,19 @@ int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
                   (long long)ldo);
 }
 
+int fvb_patchify_f32(const float* pixels, int32_t views, int32_t height,
+                     int32_t width, int32_t patch, void* out, int64_t ldo,
+                     void* stream) {
+  if (!pixels || !out || views <= 0 || patch <= 0 || height % patch ||
+      width % patch || ldo < 3 * patch * patch)
+    return fail(FVB_ERR_INVALID_ARG, "fvb_patchify_f32: bad arguments");
+  const int rows = views * (height / patch) * (width / patch);
+  return launch_k("fvb_patchify_f32", fvb::patchify_f32_kernel, dim3(rows),
+                  dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), pixels,
+                  (int)height, (int)width, (int)patch, (bf16*)out,
+                  (long long)ldo);
+}
+
 int fvb_resize_patchify(const uint8_t* images, int32_t views,
                         int32_t src_height, int32_t src_width, int32_t size,
                         int32_t patch, const float* mean3, const float* std3,

@@ -73,8 +73,14 @@ class PI0EngineB200:
 
     def __init__(self, cfg: PI0Config, weights: Dict[str, torch.Tensor],
                  prefix_len: int, device='cuda', attn_splits: int = 0,
-                 loop_impl: str = 'mega', camera_hw: Optional[tuple] = None):
+                 loop_impl: str = 'mega', camera_hw: Optional[tuple] = None,
+                 image_format: str = 'u8'):
         self.cfg = cfg
+        # 'u8': uint8 HWC camera views, normalised on the device (fast
+        # path); 'f32': the reference model's normalised float pixels
+        # [1, 3*views, H, W] (after its NormalizeImages transform)
+        assert image_format in ('u8', 'f32')
+        self.image_format = image_format
         # camera frame size (H, W) of the uint8 views handed to
         # predict_action; frames not already image_size x image_size are
         # resized on the device (OpenCV INTER_LINEAR, fused with normalise
@@ -185,6 +191,9 @@ class PI0EngineB200:
             Wv = cfg.vis_width
             B['images'] = z(cfg.n_views, self.camera_hw[0], self.camera_hw[1], 3,
                             dt=torch.uint8)
+            if self.image_format == 'f32':
+                B['pixels'] = z(cfg.n_views, 3, cfg.image_size,
+                                cfg.image_size, dt=F32)
             B['patches'] = z(R, self.P['patch_w'].shape[1])
             B['v_res'] = z(R, Wv, dt=F32)
             B['v_xn'] = z(R, Wv)
@@ -338,7 +347,9 @@ class PI0EngineB200:
         cfg, P, B = self.cfg, self.P, self.B
         Wv, R = cfg.vis_width, cfg.n_views * cfg.tokens_per_view
         hdv = Wv // cfg.vis_heads
-        if self.camera_hw == (cfg.image_size, cfg.image_size):
+        if self.image_format == 'f32':
+            ops.patchify_f32(B['pixels'], cfg.patch, B['patches'])
+        elif self.camera_hw == (cfg.image_size, cfg.image_size):
             ops.patchify(B['images'], cfg.patch, self.mean3, self.std3,
                          B['patches'])
         else:
@@ -575,7 +586,10 @@ class PI0EngineB200:
                     img_masks=None, state=None, noise=None):
         """Copy one request into the static input buffers (H2D)."""
         cfg, B = self.cfg, self.B
-        if images_u8 is not None:
+        if images_u8 is not None and self.image_format == 'f32':
+            B['pixels'].copy_(images_u8.reshape(B['pixels'].shape),
+                              non_blocking=True)
+        elif images_u8 is not None:
             B['images'].copy_(images_u8.reshape(B['images'].shape),
                               non_blocking=True)
         if lang_tokens is not None:

@@ -192,6 +192,14 @@ def patchify(images_u8: torch.Tensor, patch: int, mean3, std3,
                                   _ptr(out), out.stride(0), _stream()))
 
 
+def patchify_f32(pixels: torch.Tensor, patch: int, out: torch.Tensor) -> None:
+    """Normalised f32 pixels [views, 3, H, W] -> bf16 patch rows."""
+    V, Cc, H, W = pixels.shape
+    assert Cc == 3 and pixels.dtype == torch.float32 and pixels.is_contiguous()
+    check(_lib.lib().fvb_patchify_f32(_ptr(pixels), V, H, W, patch,
+                                      _ptr(out), out.stride(0), _stream()))
+
+
 def resize_patchify(images_u8: torch.Tensor, size: int, patch: int, mean3,
                     std3, out: torch.Tensor) -> None:
     """uint8 [V,H,W,3] of any size -> OpenCV INTER_LINEAR resize to

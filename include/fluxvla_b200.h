@@ -325,6 +325,17 @@ int fvb_patchify(const uint8_t* images, int32_t views, int32_t height,
                  int32_t width, int32_t patch, const float* mean3,
                  const float* std3, void* out, int64_t ldo, void* stream);
 
+/* Patch extraction of already normalised float pixels: f32 CHW images
+ * [views, 3, H, W] (the reference model's `images` argument, [B, 3*views,
+ * H, W] at B = 1, produced by its NormalizeImages transform) -> the bf16
+ * patch rows of fvb_patchify.
+ * Replaces: the im2col half of conv2d_embed_res (fluxvla/ops/atomic_ops.py:36)
+ * / the patch conv of SiglipVisionEmbeddings on pixel_values
+ * (fluxvla/models/backbones/visions/siglip_vit.py:121-123).               */
+int fvb_patchify_f32(const float* pixels, int32_t views, int32_t height,
+                     int32_t width, int32_t patch, void* out, int64_t ldo,
+                     void* stream);
+
 /* Fused camera preprocessing: uint8 HWC views [views, src_height,
  * src_width, 3] of any size -> resize to size x size with OpenCV's
  * INTER_LINEAR (bit-exact uint8: the same taps and 11-bit fixed-point

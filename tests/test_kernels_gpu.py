@@ -407,6 +407,13 @@ def test_patchify_embed_small_linear():
     torch.cuda.synchronize()
     close(out[:, :588], ref)
     assert out[:, 588:].abs().sum() == 0
+    # the same patch rows from already normalised f32 CHW pixels (the
+    # reference model's `images` input)
+    out2 = torch.full_like(out, 7.0)
+    ops.patchify_f32(x.contiguous(), 14, out2)
+    torch.cuda.synchronize()
+    assert torch.equal(out2[:, :588], ref.bfloat16())
+    assert out2[:, 588:].abs().sum() == 0
 
     table = rnd(1000, 64, std=0.02)
     ids = torch.randint(0, 1000, (7,), device=DEV)
