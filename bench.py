@@ -114,61 +114,149 @@ class ClockSampler:
 # CPU reference arm (oracle port of the eager reference, all host threads)
 # ---------------------------------------------------------------------------
 
-def cpu_chunk_sample(threads: int, repeats: int = 1):
-    """Time one SigLIP layer (3 views incl. patch embed / post-LN), one
-    Gemma-2B prefix layer (816 rows, bidirectional) and one expert layer
-    step (51 suffix rows over 816 cached keys, incl. suffix embedding and
-    action head) with the fp32 oracle; scale to a full chunk as
-    27*vision + 17.05*prefix + 10*18*expert (the last prefix layer only
-    computes its K/V: 0.05 of a layer).  Returns (ms per chunk, detail)."""
+def _reference_or_none():
+    """The reference's own eager modules (oracle/ref_shim.py, loaded from
+    baseline/_ref or $FLUXVLA_REF), or None when not installed."""
+    try:
+        from oracle import ref_shim
+        if ref_shim.reference_root() is None:
+            return None, None
+        return ref_shim, ref_shim.load_reference()
+    except Exception as e:  # noqa: BLE001
+        print(f'# reference modules unavailable: {e}', file=sys.stderr)
+        return None, None
+
+
+def _chunk_inputs(cfg, n_tok, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    u8 = torch.randint(0, 256, (cfg.n_views, 224, 224, 3), generator=g,
+                       dtype=torch.uint8)
+    toks = torch.randint(0, cfg.vocab, (1, n_tok), generator=g)
+    state = torch.randn(1, cfg.state_dim, generator=g)
+    noise = torch.randn(1, cfg.n_actions, cfg.action_dim, generator=g)
+    return u8, toks, state, noise
+
+
+class CpuChunk:
+    """One whole action chunk of the workload on the host cores, fp32: the
+    reference's own eager PI0FlowMatching / PI05FlowMatching
+    .predict_action when the reference is installed ('reference'), else the
+    oracle port of the same algorithm ('port').  Images are normalised as
+    the reference's NormalizeImages transform does, outside the timed call
+    for the reference (its transform runs before predict_action)."""
+
+    def __init__(self, workload: str, threads: int):
+        from fluxvla_b200.config import PI0Config, pi05_config
+        from fluxvla_b200.weights import make_weights
+        torch.set_num_threads(threads)
+        self.threads = threads
+        pi05 = workload == 'pi05'
+        self.cfg = cfg = pi05_config() if pi05 else PI0Config()
+        self.n_tok = 80 if pi05 else 48
+        t0 = time.perf_counter()
+        W = make_weights(cfg, seed=0)
+        shim, ref = _reference_or_none()
+        self.kind = 'port' if ref is None else 'reference'
+        u8, self.toks, self.state, self.noise = _chunk_inputs(cfg,
+                                                              self.n_tok)
+        self.u8 = u8
+        V = cfg.n_views
+        mean = torch.tensor(cfg.img_mean)[:, None, None]
+        std = torch.tensor(cfg.img_std)[:, None, None]
+        self.pix = ((u8.float().permute(0, 3, 1, 2) - mean) /
+                    (std + 1e-8)).reshape(1, 3 * V, 224, 224)
+        if ref is not None:
+            with shim.no_param_init():
+                self.model = shim.build_ref_model(ref, cfg)
+            shim.load_weights(self.model, cfg, W)
+            del W
+        else:
+            self.W = {k: v.float() for k, v in W.items()}
+        self.setup_s = time.perf_counter() - t0
+
+    @torch.no_grad()
+    def __call__(self):
+        if self.kind == 'reference':
+            return self.model.predict_action(
+                self.pix, self.toks, self.state,
+                img_masks=torch.ones(1, self.cfg.n_views, dtype=torch.bool),
+                lang_masks=torch.ones(1, self.n_tok, dtype=torch.bool),
+                noise=self.noise.clone())
+        from oracle import pi0_oracle as O
+        return O.predict_action(self.cfg, self.W, self.u8, self.toks,
+                                self.state, self.noise)
+
+    def sample_doc(self):
+        who = ('the reference\'s own eager {} .predict_action (fp32, loaded '
+               'unmodified from baseline/_ref through oracle/ref_shim.py)'
+               if self.kind == 'reference' else
+               'the fp32 oracle port of the eager {} path')
+        name = 'PI05FlowMatching' if self.cfg.adarms else 'PI0FlowMatching'
+        return (f'one whole config chunk per step: {who.format(name)}, '
+                f'{self.threads} host threads')
+
+
+def time_cpu_chunks(chunk: CpuChunk, n: int, warmup: int = 1):
+    for _ in range(warmup):
+        chunk()
+    ts = []
+    for _ in range(n):
+        t0 = time.perf_counter()
+        chunk()
+        ts.append(time.perf_counter() - t0)
+    return ts
+
+
+def cpu_layer0_sample():
+    """config[0] on the host: the reference's own ConditionGemmaModel layer
+    (or the oracle port) over x [1,816,2048] fp32, causal, one warm-up and
+    three timed runs.  -> (ms, kind, cores, sample)."""
     from fluxvla_b200.config import PI0Config
-    from fluxvla_b200.weights import make_weights_matching
+    from fluxvla_b200.weights import make_weights
     from oracle import pi0_oracle as O
+    threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg = PI0Config(vis_layers=1, llm_layers=1, exp_layers=1)
-    W = make_weights_matching(cfg, 0, lambda n: n != 'llm.embed')
-    g = torch.Generator().manual_seed(0)
-    pix = torch.randn(3, 3, 224, 224, generator=g)
-    x = torch.randn(1, 816, 2048, generator=g)
-    kv = [(torch.randn(1, 1, 816, 256, generator=g),
-           torch.randn(1, 1, 816, 256, generator=g))]
-    state = torch.randn(1, 32, generator=g)
-    xt = torch.randn(1, 50, 32, generator=g)
-    pad = torch.ones(1, 816, dtype=torch.bool)
-    pos = torch.arange(816)[None]
-    cos, sin = O.rope_cos_sin(pos, 256)
-    mask = O.additive_mask(torch.ones(1, 816, 816, dtype=torch.bool))
+    cfg = PI0Config(llm_layers=1)
+    W = make_weights(cfg, 0, parts=('llm',))
+    del W['llm.embed']
+    x = torch.randn(1, 816, cfg.llm_width,
+                    generator=torch.Generator().manual_seed(1))
+    shim, ref = _reference_or_none()
+    if ref is not None:
+        g = ref.cg.ConditionGemmaModel(**{
+            k: v for k, v in shim._gemma_cfg(cfg.llm_width, cfg.llm_mlp, 1,
+                                             cfg, False).items()
+            if k != 'type'}).float().eval()
+        g.config._attn_implementation = 'eager'
+        sd = {theirs[len('llm_backbone.'):]: W[ours].float()
+              for ours, theirs in shim.name_map(cfg).items() if ours in W}
+        g.load_state_dict(sd, strict=False)
+        layer = g.layers[0]
+        pos = torch.arange(816)[None]
+        pe = g.rotary_emb(x, pos)
+        causal = torch.full((816, 816), torch.finfo(torch.float32).min
+                            ).triu(1)[None, None]
 
-    def vis():
-        O.siglip_forward(pix, W, 1, cfg.vis_heads)
+        def f():
+            return layer(x, attention_mask=causal, position_ids=pos,
+                         position_embeddings=pe)[0]
+        kind = 'reference'
+    else:
+        Wf = {k: v.float() for k, v in W.items()}
 
-    def llm():
-        O.gemma_layer(x, W, 'llm.l0.', cos, sin, mask, 8, 1, 256)
-
-    def exp():
-        O.denoise_step(cfg, W, state, pad, kv, xt, torch.ones(1), 1)
-
+        def f():
+            return O.gemma_layer_causal(cfg, Wf, x)
+        kind = 'port'
     with torch.no_grad():
-        for f in (vis, llm, exp):
-            f()  # warm-up
-        res = {}
-        for name, f in (('vision_layer', vis), ('prefix_layer', llm),
-                        ('expert_layer_step', exp)):
-            ts = []
-            for _ in range(max(1, repeats)):
-                t0 = time.perf_counter()
-                f()
-                ts.append(time.perf_counter() - t0)
-            res[name] = statistics.median(ts) * 1e3
-    ms = 27 * res['vision_layer'] + 17.05 * res['prefix_layer'] + \
-        180 * res['expert_layer_step']
-    return ms, res
-
-
-SAMPLE_DOC = ('one SigLIP layer (3 views), one Gemma-2B prefix layer (816 '
-              'rows) and one expert layer step (51 rows, 816 cached keys) of '
-              'the fp32 oracle port, scaled to a chunk as 27*vision + '
-              '17.05*prefix + 180*expert; ms: ')
+        f()
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            f()
+            ts.append(time.perf_counter() - t0)
+    ms = statistics.median(ts) * 1e3
+    return ms, kind, threads, (f'median of 3 forwards of one {kind} Gemma-2B '
+                               f'layer (fp32, {threads} threads)')
 
 
 def workload_name(w):
@@ -181,32 +269,42 @@ def workload_name(w):
                 'tokens, adaRMS expert, 10 Euler steps',
         'loop': 'config[1]: PI0 action-expert loop only, 816-row prefix KV '
                 'cache, 51 suffix tokens, 10 Euler steps',
+        'layer0': 'config[0]: one Gemma-2B decoder layer, x [1,816,2048] '
+                  'f32 ~N(0,1), causal mask, positions 0..815',
     }[w]
 
 
 def run_reference(args):
+    """The reference's CPU path, timed: whole chunks of the workload (pi0 /
+    pi05 / loop use the full PI0 or PI0.5 predict_action) or config[0]
+    layers.  The number of timed chunks is capped at 5 after one warm-up
+    (a chunk takes seconds on the host); ``steps`` reports what was timed."""
     if int(os.environ.get('RANK', '0')) != 0:
         return 0
     threads = os.cpu_count() or 1
-    ms_list, detail = [], None
-    for i in range(args.warmup + args.steps):
-        ms, detail = cpu_chunk_sample(threads)
-        if i >= args.warmup:
-            ms_list.append(ms)
-    ms = statistics.median(ms_list)
-    v = 1000.0 / ms
-    sample = 'per step: ' + SAMPLE_DOC + json.dumps(
-        {k: round(x, 2) for k, x in detail.items()})
-    line = {'metric': METRIC, 'value': v, 'unit': 'chunks/s',
-            'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+    if args.workload == 'layer0':
+        ms, kind, cores, sample = cpu_layer0_sample()
+        v, unit, n = 1000.0 / ms, 'layers/s', 3
+    else:
+        chunk = CpuChunk('pi05' if args.workload == 'pi05' else 'pi0',
+                         threads)
+        n = max(1, min(args.steps, 5))
+        ts = time_cpu_chunks(chunk, n, warmup=1)
+        ms = statistics.median(ts) * 1e3
+        v, unit, kind, cores = 1000.0 / ms, 'chunks/s', chunk.kind, threads
+        sample = chunk.sample_doc() + (
+            f'; median of {n} timed chunks after 1 warm-up '
+            f'(setup {chunk.setup_s:.0f} s untimed)')
+    line = {'metric': METRIC, 'value': v, 'unit': unit,
+            'n_gpus': args.gpus, 'steps': n, 'warmup': 1,
             'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
             'impl': 'reference',
             'config': {'workload': workload_name(args.workload),
-                       'parallelism': f'replicas{args.gpus}'},
-            'cpu_baseline': {'value': v, 'unit': 'chunks/s', 'cores': threads,
-                             'kind': 'port', 'sample': sample},
-            'e2e': {'value': v, 'unit': 'chunks/s', 'h2d_bytes_per_step': 0,
+                       'parallelism': 'one host process (rank 0)'},
+            'cpu_baseline': {'value': v, 'unit': unit, 'cores': cores,
+                             'kind': kind, 'sample': sample},
+            'e2e': {'value': v, 'unit': unit, 'h2d_bytes_per_step': 0,
                     'd2h_bytes_per_step': 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -245,6 +343,9 @@ def run_b200(args):
         return float(t.item())
 
     w = args.workload
+    if w == 'layer0':
+        return run_layer0(args, world, rank, local, dev, barrier,
+                          max_over_ranks)
     depth = {} if not args.depth else dict(
         vis_layers=args.depth, llm_layers=args.depth, exp_layers=args.depth,
         vocab=4096)
@@ -387,12 +488,15 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        cms, detail = cpu_chunk_sample(threads, repeats=3)
+        chunk = CpuChunk('pi05' if w == 'pi05' else 'pi0', threads)
+        ts = time_cpu_chunks(chunk, 2, warmup=1)
+        cms = statistics.median(ts) * 1e3
         cpu = {'value': 1000.0 / cms, 'unit': 'chunks/s', 'cores': threads,
-               'kind': 'port',
-               'sample': SAMPLE_DOC + json.dumps(
-                   {k: round(x, 2) for k, x in detail.items()}),
+               'kind': chunk.kind,
+               'sample': chunk.sample_doc() + '; median of 2 timed chunks '
+                         'after 1 warm-up',
                'ms_per_chunk': cms}
+        del chunk
 
     if rank == 0:
         line = {
@@ -420,6 +524,91 @@ def run_b200(args):
             'clocks': clocks,
         }
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_layer0(args, world, rank, local, dev, barrier, max_over_ranks):
+    """config[0]: one Gemma-2B layer over 816 causal rows.  A step is one
+    layer forward (one graph replay); value = layers/s (whole job)."""
+    import torch.distributed as dist
+
+    from fluxvla_b200.config import PI0Config
+    from fluxvla_b200.layer import GemmaLayerB200
+    from fluxvla_b200.weights import make_weights
+    cfg = PI0Config(llm_layers=1)
+    W = make_weights(cfg, seed=0, parts=('llm',), device=dev)
+    del W['llm.embed']
+    S = 816
+    lay = GemmaLayerB200(cfg, W, S, device=dev)
+    x = torch.randn(1, S, cfg.llm_width,
+                    generator=torch.Generator().manual_seed(1 + rank)
+                    ).pin_memory()
+    lay.forward(x)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        lay.replay()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.6)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        lay.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = lay.forward(x)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps)
+    assert torch.isfinite(out).all()
+    peaks, peak_kind = load_peaks()
+    Wd, F, hd, H = cfg.llm_width, cfg.llm_mlp, cfg.head_dim, cfg.heads
+    params = Wd * (H + 2) * hd + H * hd * Wd + 2 * Wd * F + F * Wd
+    # causal attention: QK^T and PV over the visible half of the S x S map
+    flops = 2.0 * S * params + 2 * 2 * H * hd * S * (S + 1) / 2
+    tf = flops / (ms * 1e-3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cms, kind, cores, sample = cpu_layer0_sample()
+        cpu = {'value': 1000.0 / cms, 'unit': 'layers/s', 'cores': cores,
+               'kind': kind, 'sample': sample, 'ms_per_layer': cms}
+    if rank == 0:
+        print(json.dumps({
+            'metric': 'config[0] Gemma-2B layer forward (816 causal rows): '
+                      'layers/s', 'value': world * 1000.0 / ms,
+            'unit': 'layers/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+            'dtype': 'bf16', 'data': 'synthetic (seeded random bf16 weights, '
+                                     'x ~N(0,1))',
+            'config': {'workload': workload_name('layer0'), 'rows': S,
+                       'parallelism': f'replicas{world}',
+                       'l2': 'no flush: 220 MB of layer weights per step '
+                             '(> 126 MB L2)'},
+            'e2e': {'value': world * 1000.0 / e2e_ms, 'unit': 'layers/s',
+                    'latency_ms': e2e_ms,
+                    'h2d_bytes_per_step': S * Wd * 4,
+                    'd2h_bytes_per_step': S * Wd * 4},
+            'roofline': {'kernel': 'whole layer (7 launches)',
+                         'bound': 'tensor', 'achieved': tf,
+                         'peak': peaks['bf16_tflops'], 'unit': 'TFLOP/s',
+                         'frac': tf / peaks['bf16_tflops'],
+                         'peak_source': f'{peak_kind} burst bf16',
+                         'algorithmic_flops': flops, 'traffic': None},
+            'cpu_baseline': cpu,
+            'gpu_launches': int(lay.launches_per_call * args.steps),
+            'clocks': clocks}), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -485,7 +674,7 @@ def main():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--workload', default='pi0',
-                    choices=['pi0', 'pi05', 'loop', 'serve'])
+                    choices=['pi0', 'pi05', 'loop', 'serve', 'layer0'])
     ap.add_argument('--batches', default='1,4,16,64',
                     help='serve workload: batch sizes of the sweep')
     ap.add_argument('--no-cpu-baseline', action='store_true')

@@ -259,6 +259,15 @@ class PI0EngineB200:
             self.step_bias = torch.empty(n, We, dtype=F32, device=d)
             ops.small_linear(temb, P['action_time_in_w'][:, We:],
                              self.step_bias, bias=P['action_time_in_b'])
+            # action_in_proj is linear and feeds only the action half of
+            # action_time_mlp_in, so the two compose into one K = 32
+            # projection: h = silu(x_t Wc^T + bc + b_k) with
+            # Wc = W_time_in[:, :We] W_in and bc = W_time_in[:, :We] b_in,
+            # formed once in f32 (one launch per step instead of two)
+            Wa = P['action_time_in_w'][:, :We].float()
+            self.w_act_time = (Wa @ P['action_in_w'].float()).to(BF16)
+            self.step_bias_c = self.step_bias + (
+                Wa @ P['action_in_b'].float())[None]
         else:
             # cond_k = silu(W_out silu(W_in temb_k + b_in) + b_out)
             # (pi05_flowmatching.py:97-108); mod_k = dense(cond_k) per norm
@@ -471,11 +480,8 @@ class PI0EngineB200:
             ops.small_linear(B['x_t'], P['action_in_w'], res,
                              bias=P['action_in_b'])
         else:
-            ops.small_linear(B['x_t'], P['action_in_w'], B['a_emb'],
-                             bias=P['action_in_b'], mode=1)
-            ops.gemm(P['action_time_in_w'][:, :We], B['a_emb'], B['at_h'],
-                     swap=True, bias=self.step_bias[k], act=ACT_SILU,
-                     split_k=0, workspace=B['gemm_ws'])
+            ops.small_linear(B['x_t'], self.w_act_time, B['at_h'],
+                             bias=self.step_bias_c[k], act=ACT_SILU, mode=1)
             # K splits summed in the workspace, the last split stores
             ops.gemm(P['action_time_out_w'], B['at_h'], res[off:],
                      epilogue=EPI_F32_STORE, swap=True,

@@ -155,3 +155,24 @@ def test_stale_abort_flag_is_reported_and_cleared():
     assert ops.device_status() == 0
     again = eng.predict_action(states=state, noise=noise)
     assert (again - clean).abs().max().item() < 1e-2
+
+
+def test_config0_gemma_layer_causal_816_rows():
+    """config[0]: one Gemma-2B decoder layer, x [1, 816, 2048] ~N(0,1),
+    causal mask, positions 0..815, through the prefill kernels (captured
+    graph) against the fp32 oracle."""
+    from fluxvla_b200.layer import GemmaLayerB200
+    cfg = PI0Config(llm_layers=1)
+    W = make_weights(cfg, 21, parts=('llm',))
+    del W['llm.embed']
+    x = torch.randn(1, 816, cfg.llm_width,
+                    generator=torch.Generator().manual_seed(22))
+    lay = GemmaLayerB200(cfg, W, 816)
+    out = lay.forward(x)
+    ref = O.gemma_layer_causal(cfg, W, x)
+    check_actions(out, ref)
+    # the layer's own contribution (out - x) to 2 % of its scale
+    d, dr = out - x, ref - x
+    assert ((d - dr).norm() / dr.norm()).item() < 2e-2
+    out2 = lay.forward(x)
+    check_actions(out2, ref)
