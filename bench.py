@@ -314,6 +314,30 @@ def run_reference(args):
 # B200 arm
 # ---------------------------------------------------------------------------
 
+def captured_traffic():
+    """(bytes, note) of the expert step's DRAM traffic per launch from the
+    line ``traffic_bytes: N source_sha256: H`` of
+    profiles/expert_step_kernel.md, when H is the sha256 of the kernel
+    source (csrc/expert_mega.cuh) now; else (None, reason)."""
+    import hashlib
+    import re
+    src = os.path.join(ROOT, 'fluxvla_b200', 'csrc', 'expert_mega.cuh')
+    prof = os.path.join(ROOT, 'profiles', 'expert_step_kernel.md')
+    try:
+        with open(src, 'rb') as f:
+            sha = hashlib.sha256(f.read()).hexdigest()
+        with open(prof) as f:
+            m = re.search(r'traffic_bytes: (\d+) source_sha256: ([0-9a-f]{64})',
+                          f.read())
+    except OSError:
+        return None, 'no capture'
+    if not m:
+        return None, 'no capture'
+    if m.group(2) != sha:
+        return None, 'capture is of another kernel source (stale)'
+    return float(m.group(1)), f'ncu capture of source sha256 {sha[:12]}'
+
+
 def run_b200(args):
     import torch.distributed as dist
 
@@ -453,16 +477,17 @@ def run_b200(args):
                  for n in ('qkv', 'o_w', 'gu', 'down_w'))
     kvbytes = 2 * L * E * cfg.head_dim * 2
     ach = (wbytes + kvbytes) / t_launch / 1e9
-    # DRAM bytes (read + write) of one launch, from an ncu capture of this
-    # launch on the full config (dram__bytes_read.sum + dram__bytes_write.sum
-    # = 640.4 + 3.3 MB; PI0 / PI0.5 geometry, E = 816)
-    traffic = 643.7e6 if (L == 18 and E == 816 and not args.depth) else None
+    # DRAM bytes (read + write) of one launch from the committed ncu
+    # capture, used only while the kernel source is the one captured
+    traffic, traffic_src = captured_traffic() if (
+        L == 18 and E == 816 and not args.depth) else (None, None)
     roof = {'kernel': f'fvb::mega::expert_step_kernel ({L} expert layers of one '
                       'denoise step, persistent, 148 CTAs)',
             'bound': 'hbm', 'achieved': ach, 'peak': peaks['hbm_gbs'],
             'unit': 'GB/s', 'frac': ach / peaks['hbm_gbs'],
             'peak_source': f'{peak_kind} HBM copy (kernel timed alone)',
-            'traffic': traffic, 'launch_us': t_launch * 1e6,
+            'traffic': traffic, 'traffic_source': traffic_src,
+            'launch_us': t_launch * 1e6,
             'algorithmic_bytes_per_launch': wbytes + kvbytes}
     roof_prefill = None
     if w != 'loop':

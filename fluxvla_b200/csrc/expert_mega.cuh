@@ -95,11 +95,7 @@ struct Params {
   int nkb;         // key blocks of 64
   int trace;       // diagnostics: phase stamps of layer 0 in g_mega_trace
   int stages;      // weight ring depth in use (<= STAGES)
-  int pf_tiles;    // weight tiles prefetched into L2 ahead of the ring
-  int fold;        // 1: reshaping phases run as GEMM tails (see below)
-  unsigned long long* tile_cnt;  // [N_GEMM][MAX_MT] split arrivals per m-tile
 };
-constexpr int MAX_MT = 64;
 
 // Diagnostics: per CTA, globaltimer at worker start, then after the work
 // and after the barrier of each of the 10 phases of layer 0 (slots 24.. hold stamps inside the attention phase).
@@ -597,185 +593,6 @@ __device__ void merge_partials(const Params& p, int wtid) {
 }
 
 // ---------------------------------------------------------------------------
-// GEMM tails.  With fold = 1 the reshaping phases run in the epilogue of
-// the GEMM that produces their input instead of as phases of their own:
-// the CTA whose split of an m-tile (128 output features) arrives last on
-// that tile's counter (acq_rel, so every other split's reductions are
-// visible to it) finishes those 128 features for all tokens:
-//   QKV  -> rstd_in, bias, RoPE -> bf16 q / suffix k, v (the finalize phase)
-//   O    -> x*(1+w_post) as the gate/up operand, sum x^2 (the prep phase)
-//   GU   -> rstd_post, bias, gelu(g)*u -> the down operand (the GeGLU phase)
-//   DOWN -> x*(1+w_in of the next layer), sum x^2 (the next layer's prep)
-// and clears the accumulator tile it consumed.  Six grid barriers per layer
-// remain (QKV, attention, merge, O, gate/up, down) instead of ten.
-// ---------------------------------------------------------------------------
-// rstd of every token into shared memory (from a complete sum of squares)
-__device__ __forceinline__ void load_rstd(const Params& p, const float* ss, float* s_rstd,
-                                          int wtid) {
-  if (wtid < TOK) s_rstd[wtid] = rsqrtf(__ldcg(ss + min(wtid, p.n_tok - 1)) / p.width + p.eps);
-  bar128();
-}
-
-constexpr int TB = 4;  // token rows in flight per warp
-
-// QKV tail: features f0..f0+127 of the (H+2)*hd projection
-__device__ void tail_qkv(const Params& p, int layer, int mt, float* s_rstd, int wtid) {
-  const int H = p.heads, hd = p.hd, half = hd >> 1, ld = (H + 2) * hd;
-  const int warp = wtid >> 5, lane = wtid & 31;
-  const int f = mt * 128 + lane * 4;
-  const float* bias = p.qkv_bias ? p.qkv_bias + (long long)layer * ld : nullptr;
-  float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (bias) b4 = __ldg(reinterpret_cast<const float4*>(bias + f));
-  load_rstd(p, p.ss_in, s_rstd, wtid);
-  const bool rope = f < (H + 1) * hd;
-  const int hh = f / hd;
-  for (int t0 = warp; t0 < p.n_tok; t0 += 4 * TB) {
-    float4 a[TB];
-#pragma unroll
-    for (int u = 0; u < TB; ++u) {
-      const int t = t0 + 4 * u;
-      a[u] = t < p.n_tok ? ldcg4(p.acc_qkv + (long long)t * ld + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < TB; ++u) {
-      const int t = t0 + 4 * u;
-      if (t >= p.n_tok) break;
-      __stcg(reinterpret_cast<float4*>(p.acc_qkv + (long long)t * ld + f),
-             make_float4(0.f, 0.f, 0.f, 0.f));
-      const float r = s_rstd[t];
-      const float v0 = r * a[u].x + b4.x, v1 = r * a[u].y + b4.y;
-      const float v2 = r * a[u].z + b4.z, v3 = r * a[u].w + b4.w;
-      if (rope) {
-        const int ii = (f - hh * hd) >> 1;  // pairs (ii, ii+1)
-        const float4 cs = __ldg(reinterpret_cast<const float4*>(
-            p.rope_suf + ((long long)t * half + ii) * 2));
-        bf16* dst = hh < H ? p.qb + (long long)t * H * hd + hh * hd
-                           : p.kc + layer * p.cache_layer + (long long)(p.n_prefix + t) * hd;
-        *reinterpret_cast<__nv_bfloat162*>(dst + ii) =
-            __floats2bfloat162_rn(v0 * cs.x - v1 * cs.y, v2 * cs.z - v3 * cs.w);
-        *reinterpret_cast<__nv_bfloat162*>(dst + ii + half) =
-            __floats2bfloat162_rn(v1 * cs.x + v0 * cs.y, v3 * cs.z + v2 * cs.w);
-      } else {
-        const int d = f - (H + 1) * hd;
-        bf16* dst = p.vc + layer * p.cache_layer + (long long)(p.n_prefix + t) * hd + d;
-        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(v0, v1), pack_bf16x2(v2, v3));
-      }
-    }
-  }
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// O / DOWN tail: x columns f0..f0+127 -> bf16 x*scale, partial sum of x^2
-__device__ void tail_prep(const Params& p, const float* scale, float* ss, int mt, int wtid) {
-  const int warp = wtid >> 5, lane = wtid & 31;
-  const int f = mt * 128 + lane * 4;
-  const float4 sc = __ldg(reinterpret_cast<const float4*>(scale + f));
-  for (int t0 = warp; t0 < p.n_tok; t0 += 4 * TB) {
-    float4 a[TB];
-#pragma unroll
-    for (int u = 0; u < TB; ++u) {
-      const int t = t0 + 4 * u;
-      a[u] = t < p.n_tok ? ldcg4(p.x + (long long)t * p.width + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < TB; ++u) {
-      const int t = t0 + 4 * u;
-      if (t >= p.n_tok) break;
-      *reinterpret_cast<uint2*>(p.xs + (long long)t * p.width + f) =
-          make_uint2(pack_bf16x2(a[u].x * sc.x, a[u].y * sc.y),
-                     pack_bf16x2(a[u].z * sc.z, a[u].w * sc.w));
-      float q = a[u].x * a[u].x + a[u].y * a[u].y + a[u].z * a[u].z + a[u].w * a[u].w;
-      q = warp_sum(q);
-      if (lane == 0) atomicAdd(ss + t, q);
-    }
-  }
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// GU tail: accumulator columns f0..f0+127 = (gate, up) pairs of features
-// f0/2 .. f0/2+63 -> bf16 gelu(rs*g + bg) * (rs*u + bu)
-__device__ void tail_geglu(const Params& p, int layer, int mt, float* s_rstd, int wtid) {
-  const int warp = wtid >> 5, lane = wtid & 31;
-  const int ld = 2 * p.mlp;
-  const int f = mt * 128 + lane * 4;
-  const int i0 = f >> 1;
-  float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (p.gu_bias) b4 = __ldg(reinterpret_cast<const float4*>(p.gu_bias + (long long)layer * ld + f));
-  load_rstd(p, p.ss_post, s_rstd, wtid);
-  for (int t0 = warp; t0 < p.n_tok; t0 += 4 * TB) {
-    float4 a[TB];
-#pragma unroll
-    for (int u = 0; u < TB; ++u) {
-      const int t = t0 + 4 * u;
-      a[u] = t < p.n_tok ? ldcg4(p.acc_gu + (long long)t * ld + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < TB; ++u) {
-      const int t = t0 + 4 * u;
-      if (t >= p.n_tok) break;
-      __stcg(reinterpret_cast<float4*>(p.acc_gu + (long long)t * ld + f),
-             make_float4(0.f, 0.f, 0.f, 0.f));
-      const float r = s_rstd[t];
-      const float g0 = r * a[u].x + b4.x, u0 = r * a[u].y + b4.y;
-      const float g1 = r * a[u].z + b4.z, u1 = r * a[u].w + b4.w;
-      *reinterpret_cast<unsigned*>(p.hb + (long long)t * p.mlp + i0) =
-          pack_bf16x2(gelu_tanh_f(g0) * u0, gelu_tanh_f(g1) * u1);
-    }
-  }
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// ---------------------------------------------------------------------------
-// the CTA's weight-tile sequence (layer, GEMM, item, k-tile), in the order
-// the producer streams it; used to run an L2 prefetch ahead of the ring
-// ---------------------------------------------------------------------------
-struct TileCursor {
-  int l, gi, w, kt;  // kt = -1: first tile of item w not yet selected
-};
-
-__device__ __forceinline__ void item_ktiles(const Gemm& g, int w, int& kt0, int& kt1) {
-  const int sp = w / g.m_tiles;
-  kt0 = sp * g.kt_per;
-  kt1 = min(kt0 + g.kt_per, g.k_tiles);
-}
-
-// move the cursor onto the next existing tile (or past the last layer)
-__device__ __forceinline__ void cursor_settle(const Params& p, TileCursor& c) {
-  while (c.l < p.n_layers) {
-    const Gemm& g = p.g[c.gi];
-    if (c.w < g.items) {
-      int kt0, kt1;
-      item_ktiles(g, c.w, kt0, kt1);
-      if (c.kt < kt0) c.kt = kt0;
-      if (c.kt < kt1) return;
-      c.w += gridDim.x;
-      c.kt = -1;
-      continue;
-    }
-    c.w = blockIdx.x;
-    c.kt = -1;
-    if (++c.gi == N_GEMM) { c.gi = 0; ++c.l; }
-  }
-}
-
-__device__ __forceinline__ void prefetch_tile_l2(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
-// issue the L2 prefetch of the cursor's tile and advance the cursor
-__device__ __forceinline__ void prefetch_next(const Params& p, const CUtensorMap* const* maps,
-                                              TileCursor& c) {
-  if (c.l >= p.n_layers) return;
-  const Gemm& g = p.g[c.gi];
-  prefetch_tile_l2(maps[c.gi], c.kt * 64, c.l * g.rows + (c.w % g.m_tiles) * 128);
-  ++c.kt;
-  cursor_settle(p, c);
-}
-
-// ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(THREADS, 1)
@@ -835,7 +652,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   // all (no copy or MMA is issued) instead of returning silently wrong
   // results; the host clears the workspace after reading the status.
   __shared__ int s_skip;
-  __shared__ int s_last;  // this CTA's split arrived last on its m-tile
   if (threadIdx.x == 0) {
     s_skip = aborted(p) ? 1 : 0;
     if (s_skip && cta == 0) record_device_error(FVB_ERR_DEVICE_TIMEOUT);
@@ -859,12 +675,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- weight producer: every tile of every GEMM item, in order ----
     if (lane == 0) {
       const uint64_t pol = l2_evict_first_policy();
-      // an L2 prefetch runs pf_tiles ahead of the ring: while the ring is
-      // full during the latency-bound phases, the next GEMMs' tiles are
-      // already on their way from HBM into L2
-      TileCursor pc = {0, 0, cta, -1};
-      cursor_settle(p, pc);
-      for (int i = 0; i < p.stages + p.pf_tiles; ++i) prefetch_next(p, maps, pc);
       int it = 0;
       for (int l = 0; l < p.n_layers; ++l) {
         for (int gi = 0; gi < N_GEMM; ++gi) {
@@ -878,7 +688,6 @@ __global__ void __launch_bounds__(THREADS, 1)
               mbar_arrive_expect_tx(&full[s], A_BYTES);
               tma_load_2d_stream(ring + s * A_BYTES, maps[gi], kt * 64,
                                  l * g.rows + mt * 128, &full[s], pol);
-              if (p.pf_tiles) prefetch_next(p, maps, pc);
             }
           }
         }
@@ -936,17 +745,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       // 4 merge, 5 o_proj, 6 prep gate/up operand, 7 gate/up, 8 prep down
       // operand, 9 down
       for (int ph = 0; ph < 10; ++ph) {
-        // folded: prep / finalize / GeGLU run as GEMM tails; only the first
-        // layer keeps its prep phase (its input comes from outside)
-        if (p.fold && (ph == 2 || ph == 6 || ph == 8 || (ph == 0 && l > 0))) continue;
         if (ph == 0) {
           // clear the gate/up accumulators and ss_post (read in ph 8 of the
           // previous layer), then x*(1+w_in) and ss_in
-          if (!p.fold) {
-            for (int i = cta * 128 + wtid; i < p.n_tok * 2 * p.mlp / 4; i += G * 128)
-              reinterpret_cast<float4*>(p.acc_gu)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (cta == 0 && wtid < TOK) p.ss_post[wtid] = 0.f;
-          }
+          for (int i = cta * 128 + wtid; i < p.n_tok * 2 * p.mlp / 4; i += G * 128)
+            reinterpret_cast<float4*>(p.acc_gu)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (cta == 0 && wtid < TOK) p.ss_post[wtid] = 0.f;
           prep_scaled(p, p.in_scale + (long long)l * p.width, p.ss_in, wtid);
         } else if (ph == 2) {
           finalize_qkv(p, l, p.ss_in, s_rstd, wtid);
@@ -961,16 +765,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if (ph == 4) {  // merge; clear the QKV accumulators (read in ph 2)
           merge_partials(p, wtid);
           asm volatile("fence.proxy.async.global;" ::: "memory");
-          if (!p.fold)
-            for (int i = cta * 128 + wtid; i < p.n_tok * qkv_ld / 4; i += G * 128)
-              reinterpret_cast<float4*>(p.acc_qkv)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-          // ss_in was last read by this layer's QKV tails (or finalize) and
-          // is next summed by the down tails; ss_post was last read by the
-          // previous layer's GeGLU and is next summed by the O tails
-          if (cta == 0 && wtid < TOK) {
-            p.ss_in[wtid] = 0.f;
-            if (p.fold) p.ss_post[wtid] = 0.f;
-          }
+          for (int i = cta * 128 + wtid; i < p.n_tok * qkv_ld / 4; i += G * 128)
+            reinterpret_cast<float4*>(p.acc_qkv)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (cta == 0 && wtid < TOK) p.ss_in[wtid] = 0.f;
         } else if (ph == 6) {
           prep_scaled(p, p.post_scale + (long long)l * p.width, p.ss_post, wtid);
         } else if (ph == 8) {
@@ -1050,27 +847,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(t_empty);
-            if (p.fold && !(gi == 3 && l == p.n_layers - 1)) {
-              // count this split on its m-tile; the last one runs the tail
-              bar128();
-              if (wtid == 0) {
-                const unsigned long long old =
-                    atom_add_acq_rel64(reinterpret_cast<unsigned*>(
-                        p.tile_cnt + gi * MAX_MT + mt));
-                s_last = (old + 1) % (unsigned long long)g.splits == 0 ? 1 : 0;
-              }
-              bar128();
-              if (s_last) {
-                if (gi == 0) tail_qkv(p, l, mt, s_rstd, wtid);
-                else if (gi == 1)
-                  tail_prep(p, p.post_scale + (long long)l * p.width, p.ss_post, mt, wtid);
-                else if (gi == 2) tail_geglu(p, l, mt, s_rstd, wtid);
-                else
-                  tail_prep(p, p.in_scale + (long long)(l + 1) * p.width, p.ss_in, mt, wtid);
-                // s_rstd / s_last are reused by the next item
-                bar128();
-              }
-            }
           }
         }
         if (tr && l == 0) g_mega_trace[cta][1 + 2 * ph] = globaltimer_ns();

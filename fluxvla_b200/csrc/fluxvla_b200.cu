@@ -914,15 +914,6 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   p.nkb = (a->n_prefix + a->n_tok + 63) / 64;
   p.trace = getenv("FVB_EXPERT_TRACE") ? 1 : 0;
   p.stages = STAGES;
-  p.pf_tiles = 24;
-  p.fold = 1;
-  if (getenv("FVB_EXPERT_FOLD")) p.fold = atoi(getenv("FVB_EXPERT_FOLD")) != 0;
-  for (int i = 0; i < N_GEMM; ++i)
-    if (p.g[i].m_tiles > MAX_MT) p.fold = 0;
-  if (getenv("FVB_EXPERT_PREFETCH")) {
-    const int v = atoi(getenv("FVB_EXPERT_PREFETCH"));
-    if (v >= 0 && v <= 256) p.pf_tiles = v;
-  }
   if (getenv("FVB_EXPERT_STAGES")) {
     const int v = atoi(getenv("FVB_EXPERT_STAGES"));
     if (v >= 1 && v <= STAGES) p.stages = v;
@@ -945,7 +936,6 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   p.qb = (bf16*)take((long long)TOK * a->heads * a->head_dim * 2);
   p.xs = (bf16*)take((long long)TOK * a->width * 2);
   p.hb = (bf16*)take((long long)TOK * a->mlp * 2);
-  p.tile_cnt = (unsigned long long*)take((long long)N_GEMM * MAX_MT * 8);
   p.bar = (unsigned*)take(BAR_WORDS * 4);
   out->bytes = off;
   return FVB_OK;

@@ -24,10 +24,6 @@
  *   FVB_ATTN_TC=0        prefill attention on the mma.sync kernel instead
  *                        of the tcgen05 kernel
  *   FVB_EXPERT_STAGES=n  weight-ring depth of fvb_expert_step (1..6)
- *   FVB_EXPERT_PREFETCH=n weight tiles fvb_expert_step prefetches into L2
- *                        ahead of its ring (0 = off; default 24)
- *   FVB_EXPERT_FOLD=0    fvb_expert_step runs its reshaping steps as phases
- *                        of their own instead of GEMM tails
  *   FVB_EXPERT_TRACE=1   fvb_expert_step records per-phase timestamps
  *                        (read with fvb_expert_trace_read)
  * The trace entry points at the end of this header are diagnostics only.

@@ -168,11 +168,16 @@ def test_config0_gemma_layer_causal_816_rows():
     x = torch.randn(1, 816, cfg.llm_width,
                     generator=torch.Generator().manual_seed(22))
     lay = GemmaLayerB200(cfg, W, 816)
-    out = lay.forward(x)
     ref = O.gemma_layer_causal(cfg, W, x)
-    check_actions(out, ref)
-    # the layer's own contribution (out - x) to 2 % of its scale
-    d, dr = out - x, ref - x
-    assert ((d - dr).norm() / dr.norm()).item() < 2e-2
-    out2 = lay.forward(x)
-    check_actions(out2, ref)
+
+    def check(out):
+        # hidden states of magnitude up to ~5 (not actions): max-abs within
+        # 1 % of the output's scale and relative L2 1e-2; the layer's own
+        # contribution (out - x) within 2 % relative L2
+        err = (out - ref).abs().max().item()
+        assert err <= 1e-2 * ref.abs().max().item(), err
+        assert ((out - ref).norm() / ref.norm()).item() <= 1e-2
+        d, dr = out - x, ref - x
+        assert ((d - dr).norm() / dr.norm()).item() < 2e-2
+    check(lay.forward(x))
+    check(lay.forward(x))
