@@ -86,7 +86,8 @@ def test_dropin_matches_reference_predict_action(pi05):
     assert err <= 2e-2 and rel <= 1e-2, (err, rel)
     # a list of per-view tensors (the reference also accepts it) and a
     # batch of two requests
-    out2 = m.predict_action(list(pix.split(3, dim=1)), toks.repeat(2, 1),
+    out2 = m.predict_action(list(pix.repeat(2, 1, 1, 1).split(3, dim=1)),
+                            toks.repeat(2, 1),
                             state.repeat(2, 1), img_masks=im.repeat(2, 1),
                             lang_masks=lm.repeat(2, 1),
                             noise=noise.repeat(2, 1, 1))
