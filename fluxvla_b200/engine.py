@@ -353,7 +353,7 @@ class PI0EngineB200:
     # prefix
     # ------------------------------------------------------------------
     def _vision(self):
-        cfg, P, B = self.cfg, self.P, self.B
+        cfg, P, B, T = self.cfg, self.P, self.B, self.tiles
         Wv, R = cfg.vis_width, cfg.n_views * cfg.tokens_per_view
         hdv = Wv // cfg.vis_heads
         if self.image_format == 'f32':
@@ -384,16 +384,18 @@ class PI0EngineB200:
         for i in range(cfg.vis_layers):
             p = f'vision.l{i}.'
             ops.gemm(B['v_xn'], P[p + 'qkv_w'], qkv, bias=P[p + 'qkv_b'],
-                     block_n=192)
+                     block_n=T['vis_qkv'][0])
             ops.attention(attn)
             self._residual_gemm('vis_o', B['v_ao'], P[p + 'o_w'], B['v_res'],
-                                dict(bias=P[p + 'o_b'], split_k=2),
+                                dict(bias=P[p + 'o_b'], block_n=T['vis_o'][0],
+                                     split_k=T['vis_o'][1]),
                                 (NORM_LAYER, B['v_xn'], P[p + 'ln2_w'], P[p + 'ln2_b']))
             ops.gemm(B['v_xn'], P[p + 'fc1_w'], B['v_h'], bias=P[p + 'fc1_b'],
-                     act=ACT_GELU_TANH, block_n=192)
+                     act=ACT_GELU_TANH, block_n=T['vis_fc1'][0])
             nxt = f'vision.l{i + 1}.ln1_' if i + 1 < cfg.vis_layers else 'post_'
             self._residual_gemm('vis_fc2', B['v_h'], P[p + 'fc2_w'], B['v_res'],
-                                dict(bias=P[p + 'fc2_b'], block_n=192, split_k=4),
+                                dict(bias=P[p + 'fc2_b'], block_n=T['vis_fc2'][0],
+                                     split_k=T['vis_fc2'][1]),
                                 (NORM_LAYER, B['v_xn'], P[nxt + 'w'], P[nxt + 'b']))
         ops.gemm(B['v_xn'], P['proj_w'], B['l_res'][:R], epilogue=EPI_F32_STORE,
                  bias=P['proj_b'])
@@ -412,6 +414,11 @@ class PI0EngineB200:
     # 1: measured on the full prefill, 2 splits (102 CTAs + the combine of
     # f32 partials) cost 0.2 ms more than 51 unsplit CTAs
     prefix_attn_splits = 1
+    # (tile width, K splits) of the prefill GEMM call sites, measured on the
+    # full prefill graph
+    tiles = dict(vis_qkv=(192, 1), vis_o=(0, 2), vis_fc1=(192, 1),
+                 vis_fc2=(192, 4), llm_qkv=(0, 1), llm_o=(256, 2),
+                 llm_down=(256, 5))
 
     def _residual_gemm(self, site, a, w, res, kw, norm):
         """res += a @ w^T, then norm(res) -> bf16 (mode, out, w, b)."""
@@ -429,7 +436,7 @@ class PI0EngineB200:
             ops.norm(mode, res, out, w=nw, b=nb)
 
     def _llm(self):
-        cfg, P, B, E = self.cfg, self.P, self.B, self.E
+        cfg, P, B, E, T = self.cfg, self.P, self.B, self.E, self.tiles
         hd, H = cfg.head_dim, cfg.heads
         R = cfg.n_views * cfg.tokens_per_view if self.has_vision else 0
         ops.embed_tokens(B['tokens'][:E - R], P['embed'],
@@ -439,6 +446,7 @@ class PI0EngineB200:
             p = f'llm.l{i}.'
             kc, vc = B['kc'][i], B['vc'][i]
             ops.gemm(B['l_xn'], P[p + 'qkv'], B['l_q'], epilogue=EPI_QKV_ROPE,
+                     block_n=T['llm_qkv'][0],
                      k_out=kc[:E], v_out=vc[:E], n_heads=H, head_dim=hd,
                      rope_cs=B['rope'], positions=B['pos_prefix'])
             if i == cfg.llm_layers - 1:
@@ -451,13 +459,14 @@ class PI0EngineB200:
                 o_head_stride=hd, key_valid=B['key_valid'], n_prefix=E,
                 kv_splits=self.prefix_attn_splits, workspace=B['prefix_attn_ws']))
             self._residual_gemm('llm_o', B['l_ao'], P[p + 'o_w'], B['l_res'],
-                                dict(block_n=256, split_k=2),
+                                dict(block_n=T['llm_o'][0], split_k=T['llm_o'][1]),
                                 (NORM_GEMMA_RMS, B['l_xn'], P[p + 'post_norm'], None))
             ops.gemm(B['l_xn'], P[p + 'gu'], B['l_h'], epilogue=EPI_GEGLU,
                      block_n=256)
             # the next layer's input norm rides on the down projection
             self._residual_gemm('llm_down', B['l_h'], P[p + 'down_w'], B['l_res'],
-                                dict(block_n=256, split_k=5),
+                                dict(block_n=T['llm_down'][0],
+                                     split_k=T['llm_down'][1]),
                                 (NORM_GEMMA_RMS, B['l_xn'],
                                  P[f'llm.l{i + 1}.in_norm'], None))
 
