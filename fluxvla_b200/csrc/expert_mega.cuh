@@ -95,11 +95,10 @@ struct Params {
   int nkb;         // key blocks of 64
   int trace;       // diagnostics: phase stamps of layer 0 in g_mega_trace
   int stages;      // weight ring depth in use (<= STAGES)
-  int trace_gemm;  // diagnostics: GEMM (0..3) whose first item is stamped
 };
 
 // Diagnostics: per CTA, globaltimer at worker start, then after the work
-// and after the barrier of each of the 10 phases of layer 1 (0 if alone) (slots 24.. hold stamps inside the attention phase).
+// and after the barrier of each of the 10 phases of layer 0 (slots 24.. hold stamps inside the attention phase).
 __device__ unsigned long long g_mega_trace[256][32];
 
 // ---------------------------------------------------------------------------
@@ -689,9 +688,6 @@ __global__ void __launch_bounds__(THREADS, 1)
               mbar_arrive_expect_tx(&full[s], A_BYTES);
               tma_load_2d_stream(ring + s * A_BYTES, maps[gi], kt * 64,
                                  l * g.rows + mt * 128, &full[s], pol);
-              if (p.trace && cta < 256 && l == (p.n_layers > 1 ? 1 : 0) &&
-                  gi == p.trace_gemm && w == cta && kt == kt1 - 1)
-                g_mega_trace[cta][23] = globaltimer_ns();
             }
           }
         }
@@ -711,16 +707,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int sp = w / g.m_tiles;
             const int kt0 = sp * g.kt_per, kt1 = min(kt0 + g.kt_per, g.k_tiles);
             if (!wait_bar(p, b_full, j & 1)) goto mma_done;
-            const bool trm = p.trace && cta < 256 && l == (p.n_layers > 1 ? 1 : 0) &&
-                             gi == p.trace_gemm && w == cta;
-            if (trm) g_mega_trace[cta][27] = globaltimer_ns();
             if (!wait_bar(p, t_empty, (j & 1) ^ 1)) goto mma_done;
             tc_fence_after();
             for (int kt = kt0; kt < kt1; ++kt, ++it) {
               const int s = it % p.stages;
               if (!wait_bar(p, &full[s], (it / p.stages) & 1)) goto mma_done;
-              if (trm && kt == kt0) g_mega_trace[cta][21] = globaltimer_ns();
-              if (trm && kt == kt1 - 1) g_mega_trace[cta][22] = globaltimer_ns();
               tc_fence_after();
               const uint64_t da = smem_desc_sw128(smem_u32(ring + s * A_BYTES));
               const uint64_t db = smem_desc_sw128(bbase + (kt - kt0) * BKT_BYTES);
@@ -731,7 +722,6 @@ __global__ void __launch_bounds__(THREADS, 1)
               tc_commit(&empty[s]);
             }
             tc_commit(t_full);
-            if (trm) g_mega_trace[cta][28] = globaltimer_ns();
           }
         }
       }
@@ -749,7 +739,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     int j = 0;
     const bool tr = p.trace && wtid == 0 && cta < 256;
     uint32_t a_items = 0;  // attention items run by this CTA (a_full phases)
-    const int tl = p.n_layers > 1 ? 1 : 0;  // traced layer
     if (tr) g_mega_trace[cta][0] = globaltimer_ns();
     for (int l = 0; l < p.n_layers; ++l) {
       // phases: 0 prep QKV operand, 1 QKV, 2 finalize q/k/v, 3 attention,
@@ -772,7 +761,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           bar128();
           for (int w = cta; w < p.heads * p.nkb; w += G)
             attention_item(p, l, w, region, a_full, (a_items++) & 1, &ta_q, &ta_k, &ta_v,
-                           wtid, tr && l == tl && w == cta);
+                           wtid, tr && l == 0 && w == cta);
         } else if (ph == 4) {  // merge; clear the QKV accumulators (read in ph 2)
           merge_partials(p, wtid);
           asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -808,15 +797,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_2d(region + i * BKT_BYTES, bmap, (kt0 + i) * 64, 0, b_full);
               }
             }
-            const bool trg = tr && l == tl && gi == p.trace_gemm && w == cta;
-            if (trg) g_mega_trace[cta][31] = globaltimer_ns();
             // the lane that issued goes first: spinning lanes of a diverged
             // warp can otherwise hold it off
             __syncwarp();
             // epilogue: thread = weight row (output feature), 64 token columns
             const bool ok = wait_bar(p, t_full, j & 1);
             __syncwarp();
-            if (trg) g_mega_trace[cta][29] = globaltimer_ns();
             if (ok) {
               tc_fence_after();
               float* dst;
@@ -858,15 +844,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 __syncwarp();
               }
             }
-            if (trg) g_mega_trace[cta][30] = globaltimer_ns();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(t_empty);
           }
         }
-        if (tr && l == tl) g_mega_trace[cta][1 + 2 * ph] = globaltimer_ns();
+        if (tr && l == 0) g_mega_trace[cta][1 + 2 * ph] = globaltimer_ns();
         grid_sync(p, wtid);
-        if (tr && l == tl) g_mega_trace[cta][2 + 2 * ph] = globaltimer_ns();
+        if (tr && l == 0) g_mega_trace[cta][2 + 2 * ph] = globaltimer_ns();
       }
     }
   }

@@ -913,7 +913,6 @@ int expert_prepare(const fvb_expert_args* a, ExpertLayout* out) {
   p.scale_log2 = (1.f / sqrtf((float)a->head_dim)) * 1.4426950408889634f;
   p.nkb = (a->n_prefix + a->n_tok + 63) / 64;
   p.trace = getenv("FVB_EXPERT_TRACE") ? 1 : 0;
-  p.trace_gemm = p.trace ? atoi(getenv("FVB_EXPERT_TRACE")) & 3 : 0;
   p.stages = STAGES;
   if (getenv("FVB_EXPERT_STAGES")) {
     const int v = atoi(getenv("FVB_EXPERT_STAGES"));

@@ -376,14 +376,9 @@ int fvb_small_linear(const float* x, int64_t ldx, int32_t t, int32_t k,
  * CTAs; fvb_gemm_trace_read copies them (8 x uint64 per CTA) to the host. */
 int fvb_gemm_trace_next(void);
 int fvb_gemm_trace_read(uint64_t* host_out, int32_t max_ctas);
-/* Diagnostics: with FVB_EXPERT_TRACE=g set in the environment,
- * fvb_expert_step records per CTA (32 x uint64 globaltimer stamps each) the
- * worker start and, for layer 1 (layer 0 of a one-layer stack), the end of
- * each phase's work and of its grid barrier (slots 1..20); inside the first
- * attention item (24..26); and for the CTA's first item of GEMM g & 3
- * (0 QKV, 1 O, 2 gate/up, 3 down): first / last weight tile ready (21, 22),
- * last weight tile issued (23), B operand landed / MMAs committed (27, 28),
- * accumulator ready / epilogue done / B operand issued (29, 30, 31). */
+/* Diagnostics: with FVB_EXPERT_TRACE set in the environment,
+ * fvb_expert_step records per CTA (32 x uint64 each) the worker start and,
+ * for layer 0, the end of each phase's work and of its grid barrier. */
 int fvb_expert_trace_read(uint64_t* host_out, int32_t max_ctas);
 
 /* Status and diagnostics. */
