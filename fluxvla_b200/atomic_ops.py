@@ -68,6 +68,22 @@ def clear_cache() -> None:
     were loaded into the same buffers without a version bump)."""
     _cache.clear()
     _pos.clear()
+    _scratch_bufs.clear()
+
+
+_scratch_bufs: Dict[Tuple, torch.Tensor] = {}
+
+
+def _scratch(tag: str, rows: int, cols: int, device) -> torch.Tensor:
+    """A zero-initialised bf16 staging buffer kept per (tag, shape, device):
+    allocated on the first call of a shape only.  Callers overwrite the
+    leading columns each call; padding columns stay zero."""
+    k = (tag, rows, cols, str(device))
+    t = _scratch_bufs.get(k)
+    if t is None:
+        t = torch.zeros(rows, cols, dtype=BF16, device=device)
+        _scratch_bufs[k] = t
+    return t
 
 
 def _pad8(n: int) -> int:
@@ -110,8 +126,8 @@ def _linear(x2, w, out2, *, bias=None, act=0, res=None, gate_tok=None):
     wt = _wt(w)
     k = x2.shape[1]
     if wt.shape[1] != k:  # K not a multiple of 8: pad the activation rows
-        xp = torch.zeros(x2.shape[0], wt.shape[1], dtype=BF16, device=x2.device)
-        xp[:, :k] = x2
+        xp = _scratch('linear_x', x2.shape[0], wt.shape[1], x2.device)
+        xp[:, :k].copy_(x2)
         x2 = xp
     ops.gemm(x2, wt, out2, epilogue=EPI_BF16, act=act,
              bias=None if bias is None else _f32(bias), res=res,
@@ -254,11 +270,11 @@ def matmul_attn_v(x, V, out, head_dim):
     fused path is ``fvb_attention``)."""
     q, keys = x.shape
     kp = _pad8(keys)
-    vt = torch.zeros(head_dim, kp, dtype=BF16, device=x.device)
-    vt[:, :keys] = V.reshape(keys, head_dim).t()
+    vt = _scratch('attn_vt', head_dim, kp, x.device)
+    vt[:, :keys].copy_(V.reshape(keys, head_dim).t())
     if kp != keys:
-        xp = torch.zeros(q, kp, dtype=BF16, device=x.device)
-        xp[:, :keys] = x
+        xp = _scratch('attn_p', q, kp, x.device)
+        xp[:, :keys].copy_(x)
         x = xp
     ops.gemm(x, vt, _rows(out, head_dim), epilogue=EPI_BF16)
 

@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from . import ops
-from ._lib import EPI_BF16, EPI_F32_ACC
+from ._lib import EPI_BF16, EPI_F32_STORE
 
 
 class _TritonStyle:
@@ -56,8 +56,7 @@ def _matmul_abT_scale(q_ptr, k_ptr, out_ptr, M, N, K, scale_factor,
     k = _dense(k_ptr, N, K)
     out = _dense(out_ptr, M, N)
     if out.dtype == torch.float32:
-        out.zero_()
-        ops.gemm(q, k, out, epilogue=EPI_F32_ACC, alpha=float(scale_factor))
+        ops.gemm(q, k, out, epilogue=EPI_F32_STORE, alpha=float(scale_factor))
     else:
         ops.gemm(q, k, out, epilogue=EPI_BF16, alpha=float(scale_factor))
 

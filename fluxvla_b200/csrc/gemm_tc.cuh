@@ -436,7 +436,7 @@ __device__ __forceinline__ void epilogue_normal(const GemmDev& p, const EpiPre& 
     } else if (EPI == FVB_EPI_F32_STORE || EPI == FVB_EPI_F32_ACC) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        float y = v[j] + colv[c + j];
+        float y = (EPI == FVB_EPI_F32_STORE ? p.alpha * v[j] : v[j]) + colv[c + j];
         if (EPI == FVB_EPI_F32_ACC) y *= colv[BN + c + j];
         srow[j] = __float_as_uint(y);
       }
@@ -625,7 +625,8 @@ __device__ __forceinline__ void epilogue_tma(const GemmDev& p,
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        float y = u2f(cur[j]) + colv[c + j];
+        float y = (EPI == FVB_EPI_F32_STORE ? p.alpha * u2f(cur[j]) : u2f(cur[j])) +
+                  colv[c + j];
         if (EPI == FVB_EPI_F32_ACC) y *= colv[BN + c + j];
         w[j] = __float_as_uint(y);
       }
@@ -720,7 +721,7 @@ __device__ __forceinline__ void epilogue_swap(const GemmDev& p, const EpiPre& e,
             reinterpret_cast<bf16*>(p.out)[tt * p.ldo + f] =
                 __float2bfloat16(apply_act<ACT>(p.alpha * v[j] + e.fb));
           } else if (EPI == FVB_EPI_F32_STORE) {
-            reinterpret_cast<float*>(p.out)[tt * p.ldo + f] = v[j] + e.fb + x[j];
+            reinterpret_cast<float*>(p.out)[tt * p.ldo + f] = p.alpha * (v[j] + x[j]) + e.fb;
           } else if (EPI == FVB_EPI_F32_ACC) {
             float* o = reinterpret_cast<float*>(p.out) + tt * p.ldo + f;
             if (p.split > 1)

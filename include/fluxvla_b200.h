@@ -46,7 +46,7 @@ extern "C" {
 
 /* GEMM epilogues (fvb_gemm_args.epilogue).  t = token row, f = feature. */
 #define FVB_EPI_BF16 0      /* out_bf16[t,f] = act(alpha*acc + bias[f])      */
-#define FVB_EPI_F32_STORE 1 /* out_f32[t,f] = acc + bias[f] + row_add[t%mod,f] */
+#define FVB_EPI_F32_STORE 1 /* out_f32[t,f] = alpha*acc + bias[f] + row_add[t%mod,f] */
 #define FVB_EPI_F32_ACC 2   /* out_f32[t,f] += alpha*gate[f]*(acc + bias[f]) */
 #define FVB_EPI_GEGLU 3     /* out_bf16[t,i] = gelu_tanh(acc[2i]) * acc[2i+1] */
 #define FVB_EPI_QKV_ROPE 4  /* q -> out (RoPE), k -> k_out (RoPE), v -> v_out */
