@@ -33,6 +33,7 @@ and ``rms_matmul_scaled_qkv_rope`` (Eagle2 only) are outside this path.
 from __future__ import annotations
 
 import math
+import weakref
 from typing import Dict, Tuple
 
 import torch
@@ -44,22 +45,35 @@ from .pack import pack_geglu
 
 BF16 = torch.bfloat16
 
-_cache: Dict[Tuple, torch.Tensor] = {}
+_cache: Dict[Tuple, tuple] = {}
 _pos: Dict[Tuple, torch.Tensor] = {}
 
 
+def _owner(t: torch.Tensor) -> torch.Tensor:
+    """The tensor that owns a view's memory (the view itself otherwise)."""
+    return t._base if t._base is not None else t
+
+
 def _key(tag, *ts):
-    return (tag,) + tuple((t.untyped_storage().data_ptr(), t.storage_offset(),
-                           tuple(t.shape), tuple(t.stride()), t._version)
-                          for t in ts)
+    return (tag,) + tuple((id(_owner(t)), t.storage_offset(), tuple(t.shape),
+                           tuple(t.stride()), t._version) for t in ts)
 
 
 def _cached(tag, make, *ts):
+    """Derived copy (transpose, f32 cast, packing) of caller tensors, kept
+    while those tensors live and are unmodified.  Entries hold weak
+    references to the owning tensors: a new tensor that happens to reuse a
+    freed tensor's memory (or Python id) never hits an old entry, and
+    entries of dead tensors are dropped."""
     k = _key(tag, *ts)
-    v = _cache.get(k)
-    if v is None:
-        v = make()
-        _cache[k] = v
+    e = _cache.get(k)
+    if e is not None and all(r() is _owner(t) for r, t in zip(e[0], ts)):
+        return e[1]
+    for kk in [kk for kk, (refs, _) in _cache.items()
+               if any(r() is None for r in refs)]:
+        del _cache[kk]
+    v = make()
+    _cache[k] = ([weakref.ref(_owner(t)) for t in ts], v)
     return v
 
 

@@ -15,10 +15,12 @@ as the rest of this library does: the decoder's rotary rows start at the
 eager suffix position (prefix length + i, pi0_flowmatching.py:817-819)
 rather than the Triton path's one-off start (:458-461); everything else —
 bf16 residual streams, bf16 x_t accumulation (pi05_flowmatching_inference.py:
-310), LayerNorm eps 1e-5 — follows the Triton path.  Tolerance: the north
-star's relative L2 1e-2; max-abs within the rounding the bf16 x_t buffer
-itself adds, one bf16 unit in the last place of the largest action per
-Euler step (steps * 2^-8 * max|x|).
+310), LayerNorm eps 1e-5 — follows the Triton path.  Tolerances: (1) as the
+reference design runs it, the north star's relative L2 1e-2 and a max-abs
+within the rounding the bf16 x_t buffer itself adds, one bf16 unit in the
+last place of the largest action per Euler step (steps * 2^-8 * max|x|);
+(2) with only the Euler accumulation of x_t moved to f32, the north star's
+max-abs 2e-2 and relative L2 1e-2 — the drop-ins add no error beyond it.
 """
 import math
 
@@ -205,7 +207,12 @@ def transformer_encoder(w, b, enc, num_encoder_layers):
                        in_features=16384, out_features=2048)
 
 
-def transformer_decoder(w, b, enc, num_decoder_layers, num_steps):
+def transformer_decoder(w, b, enc, num_decoder_layers, num_steps,
+                        xt_f32=False):
+    """xt_f32: keep the Euler accumulation of x_t in an f32 copy (the
+    projections still read the bf16 buffer) instead of the reference
+    design's bf16 ``add_`` (:310); isolates the drop-ins' own error."""
+    xt = b['diffusion_noise'].float() if xt_f32 else None
     for step in range(num_steps):
         matmul_bias_silu(w['decoder_time_embeds'][step].view(1, -1),
                          w['decoder_time_mlp_in_w'], w['decoder_time_mlp_in_b'],
@@ -259,7 +266,12 @@ def transformer_decoder(w, b, enc, num_decoder_layers, num_steps):
                           w['decoder_action_out_proj_b'], b['decoder_action_buf'],
                           in_features=1024, out_features=32, BLOCK_SIZE_N=16,
                           BLOCK_SIZE_M=16, BLOCK_SIZE_K=256)
-        b['diffusion_noise'].add_(b['decoder_action_buf'], alpha=-1.0 / num_steps)
+        if xt_f32:
+            xt += b['decoder_action_buf'].float() * (-1.0 / num_steps)
+            b['diffusion_noise'].copy_(xt)
+        else:
+            b['diffusion_noise'].add_(b['decoder_action_buf'], alpha=-1.0 / num_steps)
+    return xt
 
 
 def buffers(nv, enc, dec, layers):
@@ -331,29 +343,14 @@ def test_pi05_model_on_drop_in_ops():
     rel = ((out - ref).norm() / ref.norm()).item()
     bound = steps * 2.0 ** -8 * ref.abs().max().item()
     assert rel <= 1e-2 and err <= bound, f'max-abs {err:.3e} (bound {bound:.3e}) rel-l2 {rel:.3e}'
-    # (2) against the same fp32 oracle with the reference design's bf16 x_t
-    # rounding after each Euler step (pi05_flowmatching_inference.py:310):
-    # the drop-ins themselves stay within the north star's max-abs 2e-2
-    ref_b = oracle_bf16_xt(cfg, W, imgs, toks, state, noise)[0]
-    err_b = (out - ref_b).abs().max().item()
-    rel_b = ((out - ref_b).norm() / ref_b.norm()).item()
-    assert err_b <= 2e-2 and rel_b <= 1e-2, f'max-abs {err_b:.3e} rel-l2 {rel_b:.3e}'
+    # (2) the same pipeline with x_t accumulated in f32: the drop-ins' own
+    # error is within the north star (max-abs 2e-2, relative L2 1e-2)
+    b['diffusion_noise'].copy_(noise[0])
+    out32 = transformer_decoder(w, b, enc, cfg.exp_layers, steps,
+                                xt_f32=True).cpu()
+    torch.cuda.synchronize()
+    err32 = (out32 - ref).abs().max().item()
+    rel32 = ((out32 - ref).norm() / ref.norm()).item()
+    assert err32 <= 2e-2 and rel32 <= 1e-2, f'max-abs {err32:.3e} rel-l2 {rel32:.3e}'
 
 
-def oracle_bf16_xt(cfg, W, imgs, toks, state, noise):
-    """O.predict_action with x_t rounded to bf16 after every Euler step."""
-    V = imgs.shape[0]
-    pix = O.normalize_images(imgs, [cfg.img_mean] * V, [cfg.img_std] * V)
-    pix = pix.reshape(1, 3 * V, *pix.shape[2:])
-    embs, pad, att = O.embed_prefix(cfg, W, pix, toks,
-                                    torch.ones(1, V, dtype=torch.bool),
-                                    torch.ones(toks.shape, dtype=torch.bool))
-    kv = O.prefill(cfg, W, embs, pad, att)
-    dt = torch.tensor(-1.0 / cfg.num_steps, dtype=torch.float32)
-    t = torch.tensor(1.0, dtype=torch.float32)
-    x = noise.clone().float()
-    while t >= -dt / 2:
-        v = O.denoise_step(cfg, W, state, pad, kv, x, t.expand(1))
-        x = (x + dt * v).bfloat16().float()
-        t += dt
-    return x
