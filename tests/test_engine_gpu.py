@@ -181,3 +181,46 @@ def test_config0_gemma_layer_causal_816_rows():
         assert ((d - dr).norm() / dr.norm()).item() < 2e-2
     check(lay.forward(x))
     check(lay.forward(x))
+
+
+@pytest.mark.parametrize('pi05', [False, True])
+def test_masked_view_and_padded_prompt(pi05):
+    """A camera view masked out (img_masks) and a right-padded prompt: the
+    view's 256 keys and the pad tokens are invisible to every query and the
+    positions follow cumsum(pad) - 1 (pi0_flowmatching.py:221-250,730)."""
+    kw = dict(vis_layers=1, llm_layers=2, exp_layers=2, vocab=4096)
+    cfg = pi05_config(**kw) if pi05 else PI0Config(**kw)
+    n_tok = 80 if pi05 else 48
+    W = make_weights(cfg, 13)
+    imgs, toks, state, noise = request(cfg, 14, n_tok)
+    im = torch.tensor([[True, False, True]])
+    lm = torch.ones(1, n_tok, dtype=torch.bool)
+    lm[:, n_tok - 11:] = False
+    eng = PI0EngineB200(cfg, W, prefix_len=768 + n_tok)
+    out = eng.predict_action(imgs, toks, state, img_masks=im, lang_masks=lm,
+                             noise=noise)
+    ref = O.predict_action(cfg, W, imgs, toks, state, noise, img_masks=im,
+                           lang_masks=lm)
+    check_actions(out, ref)
+    # the same engine (graph) serves an unmasked request next
+    out2 = eng.predict_action(imgs, toks, state, noise=noise)
+    check_actions(out2, O.predict_action(cfg, W, imgs, toks, state, noise))
+
+
+def test_camera_resize_path_end_to_end():
+    """Camera frames of another size (480x640) resized on the device with
+    OpenCV's INTER_LINEAR (fvb_resize_patchify) inside the captured graph,
+    against the oracle on the same frames resized by its restatement."""
+    import numpy as np
+    cfg = PI0Config(vis_layers=1, llm_layers=1, exp_layers=1, vocab=4096)
+    W = make_weights(cfg, 15)
+    g = torch.Generator().manual_seed(16)
+    frames = torch.randint(0, 256, (3, 480, 640, 3), generator=g,
+                           dtype=torch.uint8)
+    _, toks, state, noise = request(cfg, 17, 48)
+    eng = PI0EngineB200(cfg, W, prefix_len=816, camera_hw=(480, 640))
+    out = eng.predict_action(frames, toks, state, noise=noise)
+    resized = torch.stack([torch.from_numpy(np.ascontiguousarray(
+        O.resize_linear_u8(f.numpy(), 224, 224))) for f in frames])
+    ref = O.predict_action(cfg, W, resized, toks, state, noise)
+    check_actions(out, ref)
