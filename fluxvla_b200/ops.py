@@ -2,6 +2,12 @@
 on the current torch CUDA stream).  Every wrapper takes caller-allocated
 outputs, like the reference's fluxvla/ops/atomic_ops.py functions; nothing
 here allocates device memory except where a docstring says so.
+
+The per-op entry points that callers reach outside a CUDA graph (GEMM,
+norms, softmax, small linear) go through the thin torch C++ extension
+``fluxvla_b200._C`` (argument checks with TORCH_CHECK, the current stream,
+no Python-side struct building); the others through the ctypes binding of
+the same library.  Both are required: there is no fallback.
 """
 from __future__ import annotations
 
@@ -17,6 +23,23 @@ from ._lib import (ACT_NONE, EPI_BF16, EPI_F32_ACC, EPI_F32_STORE,
 
 BF16 = torch.bfloat16
 F32 = torch.float32
+
+_ext = None
+
+
+def _C():
+    """The torch extension (built next to the library by
+    ``python -m fluxvla_b200.build``)."""
+    global _ext
+    if _ext is None:
+        try:
+            from . import _C as ext
+        except ImportError as e:
+            raise RuntimeError(
+                'fluxvla_b200._C is missing: build it with `python -m '
+                'fluxvla_b200.build` (there is no fallback path)') from e
+        _ext = ext
+    return _ext
 
 
 def _ptr(t: Optional[torch.Tensor]) -> int:
@@ -62,42 +85,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
     [m, n] row-major views) make the bf16 epilogue out = res + gate_tok *
     act(alpha*acc + bias); ``rope_interleaved`` stores rotated q / k with each
     rotary pair adjacent."""
-    lda = _rowmajor(a, 'a', BF16)
-    ldb = _rowmajor(b, 'b', BF16)
-    if a.shape[1] != b.shape[1]:
-        raise ValueError(f'K mismatch {a.shape} {b.shape}')
-    out_dtype = F32 if epilogue in (EPI_F32_STORE, EPI_F32_ACC) else BF16
-    ldo = _rowmajor(out, 'out', out_dtype)
-    for t, n in ((bias, 'bias'), (gate, 'gate')):
-        if t is not None and (t.dtype != F32 or not t.is_contiguous()):
-            raise TypeError(f'{n}: expected contiguous float32')
-    args = GemmArgs(a=_ptr(a), lda=lda, b=_ptr(b), ldb=ldb, m=a.shape[0],
-                    n=b.shape[0], k=a.shape[1], swap=int(swap),
-                    epilogue=epilogue, act=act, split_k=split_k,
-                    block_n=block_n, out=_ptr(out), ldo=ldo, bias=_ptr(bias),
-                    gate=_ptr(gate), alpha=alpha, row_add=_ptr(row_add),
-                    row_add_mod=row_add_mod, k_out=_ptr(k_out),
-                    v_out=_ptr(v_out),
-                    ld_kv=0 if k_out is None else k_out.stride(0),
-                    n_heads=n_heads, head_dim=head_dim, rope_cs=_ptr(rope_cs),
-                    positions=_ptr(positions), workspace=_ptr(workspace),
-                    workspace_bytes=0 if workspace is None else
-                    workspace.numel() * workspace.element_size(),
-                    pair=int(pair), res=_ptr(res),
-                    ld_res=0 if res is None else _rowmajor(res, 'res', BF16),
-                    gate_tok=_ptr(gate_tok),
-                    ld_gate_tok=0 if gate_tok is None else
-                    _rowmajor(gate_tok, 'gate_tok', BF16),
-                    rope_interleaved=int(rope_interleaved))
-    if norm is not None:
-        mode, nout, nw, nb, eps, sync = norm
-        args.norm_mode = mode
-        args.norm_out = _ptr(nout)
-        args.ld_norm_out = _rowmajor(nout, 'norm_out', BF16)
-        args.norm_w, args.norm_b = _ptr(nw), _ptr(nb)
-        args.norm_eps = eps
-        args.norm_sync = _ptr(sync)
-    check(_lib.lib().fvb_gemm(C.byref(args), _stream()))
+    nm, nout, nw, nb, neps, nsync = norm if norm is not None else (
+        0, None, None, None, 0.0, None)
+    _C().gemm(a, b, out, epilogue, swap, act, bias, gate, alpha, split_k,
+              block_n, row_add, row_add_mod, k_out, v_out, n_heads, head_dim,
+              rope_cs, positions, workspace, pair, res, gate_tok,
+              rope_interleaved, nm, nout, nw, nb, neps, nsync)
 
 
 def gemm_workspace_bytes(m: int, n: int, swap: bool, epilogue: int) -> int:
@@ -146,39 +139,19 @@ def norm_bf16(mode: int, x: torch.Tensor, out: torch.Tensor, *, w=None,
     """Norm of bf16 rows (fvb_norm_bf16): NORM_RMS (no weight), NORM_LAYER
     (w, b bf16) or NORM_ADA_STYLE (style bf16 row: scale | shift | gate;
     the gate goes to gate_out for every row)."""
-    ld_in = _rowmajor(x, 'x', BF16)
-    ld_out = _rowmajor(out, 'out', BF16)
-    rows, dim = x.shape
-    check(_lib.lib().fvb_norm_bf16(
-        mode, _ptr(x), ld_in, _ptr(out), ld_out, rows, dim, _ptr(w), _ptr(b),
-        _ptr(style), _ptr(gate_out),
-        0 if gate_out is None else _rowmajor(gate_out, 'gate_out', BF16),
-        eps, _stream()))
+    _C().norm_bf16(mode, x, out, w, b, style, gate_out, eps)
 
 
 def softmax_rows(logits: torch.Tensor, out: torch.Tensor, *, n_prefix: int,
                  valid_prefix: torch.Tensor) -> None:
     """bf16 out = softmax over the attended keys of f32 logits rows
     (fvb_softmax_rows); valid_prefix: int32 device tensor of one value."""
-    if valid_prefix.dtype != torch.int32 or not valid_prefix.is_cuda:
-        raise TypeError('valid_prefix: expected an int32 CUDA tensor')
-    ld_in = _rowmajor(logits, 'logits', F32)
-    ld_out = _rowmajor(out, 'out', BF16)
-    rows, keys = logits.shape
-    check(_lib.lib().fvb_softmax_rows(_ptr(logits), ld_in, rows, keys, n_prefix,
-                                      _ptr(valid_prefix), _ptr(out), ld_out,
-                                      _stream()))
+    _C().softmax_rows(logits, out, n_prefix, valid_prefix)
 
 
 def norm(mode: int, x: torch.Tensor, out: torch.Tensor, *, w=None, b=None,
          mod=None, eps: float = 1e-6) -> None:
-    ld_in = _rowmajor(x, 'x', F32)
-    out_f32 = out.dtype == F32
-    ld_out = _rowmajor(out, 'out', F32 if out_f32 else BF16)
-    rows, dim = x.shape
-    check(_lib.lib().fvb_norm(mode, _ptr(x), ld_in, _ptr(out), ld_out,
-                              int(out_f32), rows, dim, _ptr(w), _ptr(b),
-                              _ptr(mod), eps, _stream()))
+    _C().norm(mode, x, out, w, b, mod, eps)
 
 
 def patchify(images_u8: torch.Tensor, patch: int, mean3, std3,
@@ -224,11 +197,7 @@ def small_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *,
                  alpha: float = 1.0, k: Optional[int] = None) -> None:
     """y = act(x @ w[:, :k]^T + bias); mode 0 store f32, 1 store bf16,
     2 out += alpha*y (f32)."""
-    T, K = x.shape[0], (k or x.shape[1])
-    check(_lib.lib().fvb_small_linear(_ptr(x), x.stride(0), T, K, _ptr(w),
-                                      w.stride(0), w.shape[0], _ptr(bias),
-                                      act, mode, alpha, _ptr(out),
-                                      out.stride(0), _stream()))
+    _C().small_linear(x, w, out, bias, act, mode, alpha, k or 0)
 
 
 def probe_wait_timeout(limit_s: float = 0.05) -> bool:

@@ -4,6 +4,8 @@ import ctypes
 import os
 import re
 
+import pytest
+
 from fluxvla_b200 import _lib
 
 HDR = os.path.join(os.path.dirname(os.path.dirname(__file__)), 'include',
@@ -37,3 +39,22 @@ def test_invalid_arguments_return_errors_without_gpu():
     args = _lib.GemmArgs()
     rc = L.fvb_gemm(ctypes.byref(args), None)
     assert rc == 1 and b'NULL' in L.fvb_last_error()
+
+
+def test_torch_extension_loads_and_reports_errors():
+    """fluxvla_b200._C (the thin torch extension over the C ABI) loads with
+    the library, exposes the op entry points, raises ValueError for a bad
+    argument and RuntimeError (with the library's message) for an error the
+    C ABI returns — without a GPU."""
+    import torch
+
+    from fluxvla_b200 import ops
+    ext = ops._C()
+    for name in ('gemm', 'norm', 'norm_bf16', 'softmax_rows', 'small_linear'):
+        assert callable(getattr(ext, name))
+    with pytest.raises(RuntimeError, match='status is NULL'):
+        ext.error_path_probe()
+    with pytest.raises(ValueError, match='must be a CUDA tensor'):
+        ops.norm(0, torch.zeros(2, 128), torch.zeros(2, 128))
+    with pytest.raises(ValueError, match='expected'):
+        ops.norm(0, torch.zeros(2, 128, dtype=torch.int32), torch.zeros(2, 128))
